@@ -1,0 +1,318 @@
+"""Benchmark of the B200 Whisper decoder token loop.
+
+One "step" is one whole Decode of the batch: cross K/V precompute for every
+utterance, then the token loop (224 steps, beam 5 by default) on the GPU.
+Workload (default): BASELINE.json configs[4], large-v3-shaped decoder
+(d=1280, 32 layers, 20 heads, vocab 51866), Q8_0 weights from seeded
+N(0, 0.02), 64 utterances per GPU with synthetic N(0,1) encoder outputs
+[1500, 1280], beam 5, 224 steps (EOT suppressed so every utterance runs the
+full length), CORRECT-mode decoding. N GPUs (torchrun) each decode their own
+64 utterances: weak scaling, no collective on the token loop.
+
+  value : decoder tokens/s (utterance-steps/s, beams not counted), inputs
+          resident in HBM, device time from CUDA events on the job's stream,
+          max over ranks
+  e2e   : same metric through the public C-ABI job API with pinned host
+          encoder outputs uploaded and tokens read back every step
+  --impl reference : the CPU restatement of whisper.go's decoder (oracle),
+          timed on the host cores, on a bounded sample of the same workload
+"""
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "whisper.go_b200"))
+
+CONFIGS = {
+    1: dict(name="tiny.en-shaped Q8_0 greedy", V=51864, d=384, L=4, H=6, qtype="Q8_0", beam=1, U=1),
+    2: dict(name="base-shaped Q4_0 greedy", V=51865, d=512, L=6, H=8, qtype="Q4_0", beam=1, U=1),
+    3: dict(name="small-shaped Q5_1 beam5", V=51865, d=768, L=12, H=12, qtype="Q5_1", beam=5, U=1),
+    4: dict(name="medium-shaped Q5_0 beam5 x8", V=51865, d=1024, L=24, H=16, qtype="Q5_0", beam=5, U=8),
+    5: dict(name="large-v3-shaped Q8_0 beam5 x64", V=51866, d=1280, L=32, H=20, qtype="Q8_0", beam=5, U=64),
+}
+PROMPT = [50258, 50259, 50357, 50363]
+T_ENC, STEPS_PER_DECODE, SEED = 1500, 224, 20261201
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=5)
+    ap.add_argument("--utterances", type=int, default=0, help="per GPU (default: the config's)")
+    ap.add_argument("--tokens", type=int, default=STEPS_PER_DECODE)
+    ap.add_argument("--mode", default="correct", choices=["correct", "ref_compat"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-steps", type=int, default=2)
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+class Dist:
+    """torch.distributed plumbing: barrier and max over ranks (no data-path collective)."""
+
+    def __init__(self, world, local):
+        self.world = world
+        self.pg = None
+        if world > 1:
+            import datetime
+            import torch
+            import torch.distributed as td
+            torch.cuda.set_device(local)
+            td.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
+                                  device_id=torch.device("cuda", local))
+            self.td, self.torch, self.local = td, torch, local
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            self.td.barrier()
+
+    def max(self, x):
+        if not self.pg:
+            return x
+        t = self.torch.tensor([float(x)], device="cuda:%d" % self.local, dtype=self.torch.float64)
+        self.td.all_reduce(t, op=self.td.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, x):
+        if not self.pg:
+            return x
+        t = self.torch.tensor([float(x)], device="cuda:%d" % self.local, dtype=self.torch.float64)
+        self.td.all_reduce(t, op=self.td.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.td.destroy_process_group()
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), "--query-gpu=" + self.FIELDS,
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.th = threading.Thread(target=self._read, daemon=True)
+            self.th.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.th.join(timeout=2)
+        sm, mx, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+                power.append(float(r[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+def cpu_baseline(model, cfg, U, args, n_ctx, threads):
+    """The oracle (CPU restatement of the reference decoder) on a bounded sample."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle  # test infrastructure: the timed CPU baseline only
+    import wgdec
+    params = wgdec.DecoderParams(prompt=PROMPT, beam_size=cfg["beam"], max_tokens=args.tokens,
+                                 mode=wgdec.MODE_REF_COMPAT, suppress_eot=True)
+    n_utt = min(U, threads)
+    sec, toks = oracle.bench_steps(model, n_utt, T_ENC, params, args.cpu_sample_steps, threads)
+    return {"value": toks / sec if sec > 0 else None, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": "%d utterances x %d token steps (beam %d, REF_COMPAT arithmetic, GEMVs serial per "
+                      "hypothesis as in the reference, cross K/V cached) on %d threads: %.1f s"
+                      % (n_utt, args.cpu_sample_steps, cfg["beam"], threads, sec)}
+
+
+def run_reference(args, cfg, rank, world):
+    if rank != 0:
+        return 0
+    import wgdec
+    threads = os.cpu_count() or 1
+    model = wgdec.SyntheticModel(cfg["V"], cfg["d"], cfg["H"], cfg["L"], 448, cfg["qtype"], seed=SEED)
+    U = args.utterances or cfg["U"]
+    vals = []
+    for i in range(args.warmup + args.steps):
+        cb = cpu_baseline(model, cfg, U, args, 448, threads)
+        if i >= args.warmup:
+            vals.append(cb)
+    v = statistics.median([c["value"] for c in vals])
+    line = {"impl": "reference", "metric": "decoder tokens/s", "value": v, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init weights, N(0,1) encoder)",
+            "config": {"workload": "config %d: %s" % (args.config, cfg["name"]), "utterances_per_gpu": U,
+                       "beam": cfg["beam"], "tokens": args.tokens},
+            "cpu_baseline": {"kind": "port", "cores": threads, "sample": vals[-1]["sample"], "value": v},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    cfg = CONFIGS[args.config]
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, cfg, rank, world)
+    import numpy as np
+    import wgdec
+    dist = Dist(world, local)
+    U = args.utterances or cfg["U"]
+    mode = wgdec.MODE_CORRECT if args.mode == "correct" else wgdec.MODE_REF_COMPAT
+    model = wgdec.SyntheticModel(cfg["V"], cfg["d"], cfg["H"], cfg["L"], 448, cfg["qtype"], seed=SEED)
+    dec = wgdec.WhisperDecoder(model, devices=[local])
+    # encoder outputs of this rank's utterances, in pinned host memory
+    import torch
+    host = torch.empty((U, T_ENC, cfg["d"]), dtype=torch.float32, pin_memory=True)
+    hnp = host.numpy()
+    for u in range(U):
+        hnp[u] = model.encoder_output(rank * U + u, T_ENC)
+    encs = [hnp[u] for u in range(U)]
+    params = wgdec.DecoderParams(prompt=PROMPT, beam_size=cfg["beam"], max_tokens=args.tokens, mode=mode,
+                                 suppress_eot=True)
+    job = wgdec.Job(dec, U, T_ENC, params)
+    job.upload(encs)  # resident in HBM before the timed region
+
+    def decode_once():
+        job.start()
+        job.run()
+
+    for _ in range(args.warmup):
+        decode_once()
+    dist.barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    launches0 = wgdec.kernel_launch_count()
+    job.timer_start()
+    for _ in range(args.steps):
+        decode_once()
+    ms = job.timer_stop()
+    launches = wgdec.kernel_launch_count() - launches0
+    clk = clocks.stop()
+    toks, lens, _ = job.result()
+    tokens_per_decode = float(np.sum(lens - len(PROMPT)))
+    dist.barrier()
+    ms_max = dist.max(ms)
+    total_tokens = dist.sum(tokens_per_decode * args.steps)
+    value = total_tokens / (ms_max / 1e3)
+
+    # roofline: per-class device time of one step's launches (CUDA events on the job stream)
+    peak, peak_kind = peaks()
+    classes = {}
+    steps_done, rows, _ = job.stats()
+    per_step_launches = {"gemv": 6 * cfg["L"], "self_attn": cfg["L"], "cross_attn": cfg["L"], "logits": 1}
+    for k in ("gemv", "self_attn", "cross_attn", "logits"):
+        t, b = job.time_kernel(k, iters=3)
+        classes[k] = {"ms_per_launch": t, "bytes_per_launch": b, "gbs": b / (t * 1e6) if t > 0 else None,
+                      "ms_per_step": t * per_step_launches[k]}
+    dom = max(classes, key=lambda k: classes[k]["ms_per_step"])
+    dk = classes[dom]
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": dk["gbs"], "peak": peak, "unit": "GB/s",
+                "frac": dk["gbs"] / peak if dk["gbs"] else None, "traffic": None,
+                "peak_kind": peak_kind, "classes": classes}
+
+    job.close()  # free its KV caches before the end-to-end job allocates its own
+    # end to end through the public API: pinned host -> device, decode, tokens back
+    e2e = None
+    if not args.no_e2e:
+        e2e_job = wgdec.Job(dec, U, T_ENC, params)
+        e2e_job.upload(encs)
+        e2e_job.start()
+        e2e_job.run()
+        e2e_job.result()
+        dist.barrier()
+        e2e_job.timer_start()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_job.upload(encs)
+            e2e_job.start()
+            e2e_job.run()
+            t2, l2, _ = e2e_job.result()
+        e_ms = e2e_job.timer_stop()
+        wall = (time.perf_counter() - t0) * 1e3
+        e_ms = dist.max(max(e_ms, wall))
+        e2e = {"value": total_tokens / (e_ms / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(U * T_ENC * cfg["d"] * 4),
+               "d2h_bytes_per_step": int(t2.nbytes + l2.nbytes + 4 * U)}
+        e2e_job.close()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(model, cfg, U, args, 448, os.cpu_count() or 1)
+
+    if rank == 0:
+        line = {"metric": "decoder tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16xf16->f32",
+                "data": "synthetic (seeded random-init weights, N(0,1) encoder outputs)",
+                "config": {"workload": "config %d: %s" % (args.config, cfg["name"]), "utterances_per_gpu": U,
+                           "beam": cfg["beam"], "rows_per_step": rows, "tokens_per_decode": args.tokens,
+                           "mode": args.mode, "kv_dtype": "f16", "t_enc": T_ENC,
+                           "l2": "inputs larger than L2 (per-step KV + weights >> 126 MB)",
+                           "parallelism": "dp%d (utterances, no collective)" % world},
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+                "gpu_launches": int(launches)}
+        print(json.dumps(line), flush=True)
+    dec.close()
+    dist.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,207 @@
+/*
+ * wg_decoder.h — C ABI of the B200 (sm_100a) Whisper decoder token loop.
+ *
+ * This library replaces, below the Go interface
+ *     model.Decoder.Decode(ctx, encoderOut ml.Tensor, params DecoderParams)
+ *         (internal/model/interfaces.go:22-25)
+ * the CPU implementation in internal/model/decoder.go (WhisperDecoder,
+ * decoder.go:61-82) and the tensor ops it calls (internal/ml/matmul_q8.go,
+ * attention.go, ops.go). A cgo package binds these symbols; see
+ * INTEGRATION.md for the binding.
+ *
+ * Conventions
+ *  - Every function returns an int status (WG_OK == 0). No C++ exception
+ *    crosses this boundary. wg_last_error() returns the text of the last
+ *    error raised on the calling thread.
+ *  - All pointers in descriptors are HOST pointers and are borrowed: the
+ *    library copies what it needs before the call returns.
+ *  - Matrices are passed exactly as gguf.FileLike.TensorRaw returns them
+ *    (internal/gguf/gguf.go:228-246): raw little-endian GGUF block bytes,
+ *    shape[0] = rows (output features), shape[1] = cols (input features).
+ *  - A wg_job is not re-entrant; distinct jobs may run concurrently.
+ */
+#ifndef WG_DECODER_H
+#define WG_DECODER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+enum {
+  WG_OK = 0,
+  WG_ERR_INVALID = 1,     /* bad argument / shape (reference: ErrShapeMismatch, fmt.Errorf) */
+  WG_ERR_CUDA = 2,        /* CUDA runtime error */
+  WG_ERR_OOM = 3,         /* device allocation failed */
+  WG_ERR_UNSUPPORTED = 4, /* feature of DecoderParams not implemented on the device */
+  WG_ERR_CANCELLED = 5,   /* wg_job_cancel() was called (context.Canceled) */
+  WG_ERR_TIMEOUT = 6,     /* host watchdog deadline passed */
+  WG_ERR_INJECTED = 7,    /* host-side fault injection (WG_FAULT_INJECT) */
+  WG_ERR_NO_DEVICE = 8,   /* no CUDA device / library built without one */
+  WG_ERR_DEVICE_FLAG = 9  /* a kernel's bounded wait expired and set the error word */
+};
+
+/* ---- GGUF tensor types (internal/gguf/gguf.go dtype ids; ml/matmul_q8.go:15-32) */
+enum {
+  WG_QTYPE_F32 = 0,
+  WG_QTYPE_F16 = 1,
+  WG_QTYPE_Q4_0 = 2,
+  WG_QTYPE_Q4_1 = 3,
+  WG_QTYPE_Q5_0 = 6,
+  WG_QTYPE_Q5_1 = 7,
+  WG_QTYPE_Q8_0 = 8
+};
+
+/* ---- decode semantics -------------------------------------------------- */
+enum {
+  /* The reference's literal behaviour (internal/model/decoder.go):
+   * forward() processes only the last token (decoder.go:750-757, no prompt
+   * prefill), and the Tq=1 causal mask leaves only KV slot 0 visible
+   * (ml/attention.go:250-256). Beam hypotheses reset their KV cache every
+   * step (decoder.go:593, resetDecoderState :372-386). */
+  WG_MODE_REF_COMPAT = 0,
+  /* Standard Whisper decoding: the prompt is prefilled and self-attention
+   * covers positions 0..pos; beam hypotheses keep their KV history. */
+  WG_MODE_CORRECT = 1
+};
+
+/* One weight matrix, as TensorRaw returns it. */
+typedef struct wg_matrix {
+  uint32_t qtype;   /* WG_QTYPE_* */
+  int32_t rows;     /* output features (TensorRaw shape[0]) */
+  int32_t cols;     /* input features  (TensorRaw shape[1]) */
+  const void* data; /* rows * row_bytes(qtype, cols) bytes */
+} wg_matrix;
+
+/* One decoder block (decoderBlock, decoder.go:43-58; loaded at :203-292). */
+typedef struct wg_layer_desc {
+  const float* self_ln_w;  const float* self_ln_b;      /* [d] */
+  wg_matrix self_q;  const float* self_q_b;             /* [d,d], [d] */
+  wg_matrix self_k;                                     /* [d,d] no bias */
+  wg_matrix self_v;  const float* self_v_b;
+  wg_matrix self_o;  const float* self_o_b;
+  const float* cross_ln_w; const float* cross_ln_b;
+  wg_matrix cross_q; const float* cross_q_b;
+  wg_matrix cross_k;                                    /* no bias */
+  wg_matrix cross_v; const float* cross_v_b;
+  wg_matrix cross_o; const float* cross_o_b;
+  const float* mlp_ln_w;   const float* mlp_ln_b;
+  wg_matrix mlp0;    const float* mlp0_b;               /* [4d,d], [4d] */
+  wg_matrix mlp2;    const float* mlp2_b;               /* [d,4d], [d] */
+} wg_layer_desc;
+
+/* Decoder hyper-parameters and weights (WhisperDecoder, decoder.go:61-82;
+ * hyper-parameters from metadata keys read at decoder.go:101-105). */
+typedef struct wg_model_desc {
+  int32_t n_vocab;     /* whisper.vocab.size */
+  int32_t n_state;     /* whisper.decoder.embedding_length (d) */
+  int32_t n_head;      /* whisper.decoder.attention.head_count */
+  int32_t n_layer;     /* whisper.decoder.layer_count */
+  int32_t n_text_ctx;  /* whisper.decoder.context_length */
+  int32_t eot;         /* end-of-text id; 50256 without a vocabulary (decoder.go:173) */
+  wg_matrix token_embedding;          /* [n_vocab, d]; tied with the logits projection */
+  const float* positional_embedding;  /* [n_text_ctx, d] fp32 */
+  const float* ln_w;  const float* ln_b;  /* final LayerNorm [d] */
+  const wg_layer_desc* layers;        /* n_layer entries */
+} wg_model_desc;
+
+/* The DecoderParams fields the reference decoder reads
+ * (internal/model/interfaces.go:75-90), plus two switches of this build. */
+typedef struct wg_decode_params {
+  int32_t beam_size;        /* <= 1: greedy (decoder.go:406) */
+  float temperature;        /* 0 means 1.0 (decoder.go:416-419, :530-533) */
+  int32_t attempt;          /* temperature-schedule attempt: T += 0.2*attempt (decoder.go:435,:537) */
+  float logprob_thold;      /* > 0 with !no_fallback enables top-p fallback: WG_ERR_UNSUPPORTED */
+  float no_speech_thold;    /* used by suppress_nst (decoder.go:1016-1034) */
+  int32_t no_fallback;
+  int32_t max_tokens;       /* <= 0: n_text_ctx; capped at n_text_ctx - P (decoder.go:421-430) */
+  int32_t suppress_nst;
+  int32_t mode;             /* WG_MODE_REF_COMPAT or WG_MODE_CORRECT */
+  int32_t suppress_eot;     /* 1: EOT never selected (fixed-length benchmark runs); 0: reference */
+} wg_decode_params;
+
+typedef struct wg_model wg_model;
+typedef struct wg_job wg_job;
+
+/* ---- library / errors -------------------------------------------------- */
+int wg_last_error(char* buf, size_t len);
+int wg_device_count(int* n);
+/* Number of our own kernels launched by this process so far (all devices). */
+int wg_kernel_launch_count(int64_t* n);
+
+/* ---- model ------------------------------------------------------------- */
+/* Replaces model.NewDecoder (internal/model/decoder.go:97-303): uploads one
+ * replica of the weights to each listed device (n_dev >= 1). */
+int wg_model_create(const wg_model_desc* desc, const int* devices, int n_dev, wg_model** out);
+int wg_model_destroy(wg_model* m);
+/* Device bytes of one replica's weights (quant blocks as uploaded). */
+int wg_model_weight_bytes(const wg_model* m, int64_t* bytes);
+
+/* ---- decode jobs (replaces WhisperDecoder.Decode, decoder.go:401-410) --- */
+/* Allocates device state for U utterances of T_enc encoder frames with a
+ * prompt of P tokens shared by every utterance. Utterances are sharded
+ * round-robin over the model's devices. */
+int wg_job_create(wg_model* m, int U, int T_enc, const int32_t* prompt, int P,
+                  const wg_decode_params* params, wg_job** out);
+/* Host -> device copy of U encoder outputs, each [T_enc, d] fp32 row-major
+ * (enc[u] points at utterance u). */
+int wg_job_upload_encoder(wg_job* j, const float* const* enc);
+/* Cross K/V precompute for every layer, prompt prefill (CORRECT mode) and
+ * reset of the beam / token state. Must follow an upload. */
+int wg_job_start(wg_job* j);
+/* Runs up to max_steps token steps on all devices (CUDA-graph replays).
+ * *done = 1 when every utterance has finished. Returns WG_ERR_CANCELLED if
+ * wg_job_cancel was called before or during the call. */
+int wg_job_step(wg_job* j, int max_steps, int* done);
+/* tokens: U x (P + max_tokens) int32 (prompt included, like the reference's
+ * final token slice), lens: U, scores: U (beam log-prob sum; 0 for greedy). */
+int wg_job_result(wg_job* j, int32_t* tokens, int32_t* lens, float* scores);
+int wg_job_cancel(wg_job* j);
+/* Device timer on the job's own stream(s): which = 0 records the start
+ * event, which = 1 records the stop event, waits, and returns in *ms the
+ * elapsed device time (max over the job's devices). */
+int wg_job_timer(wg_job* j, int which, double* ms);
+int wg_job_destroy(wg_job* j);
+/* Token steps executed so far (max over utterances) and rows per step. */
+int wg_job_stats(const wg_job* j, int* steps_done, int* rows, int* max_tokens);
+
+/* One call = the whole Decode for U utterances: create, upload, start,
+ * step to completion, result, destroy. */
+int wg_decode(wg_model* m, const float* const* enc, int U, int T_enc,
+              const int32_t* prompt, int P, const wg_decode_params* params,
+              int32_t* tokens, int32_t* lens, float* scores);
+
+/* Teacher-forced logits for U utterances (one row each): step s processes
+ * the last token of prompt+forced[u][0..s) exactly as decodeGreedy's forward
+ * calls do (decoder.go:441-447) and writes logits[(s*U + u)*n_vocab ...]
+ * (before the repetition penalty). forced: U x n_forced. mode: WG_MODE_*. */
+int wg_teacher_forced_logits(wg_model* m, const float* const* enc, int U, int T_enc,
+                             const int32_t* prompt, int P,
+                             const int32_t* forced, int n_forced, int mode,
+                             float* logits);
+
+/* ---- unit entry points (kernel-level parity) ---------------------------- */
+/* Device dequantisation of raw GGUF blocks through the device weight layout
+ * (gguf/dequant.go:92-201). out: n fp32 values. Bit-exact with the reference. */
+int wg_dequant_test(uint32_t qtype, const void* raw, int64_t n, float* out);
+/* out[m, rows] = x[m, cols] * dequant(W[rows, cols])^T with the device GEMV
+ * (path 0: auto, 1: SIMT GEMV, 2: tcgen05 tensor-core tiles).
+ * Replaces ml.MatMulQuantTransBInto (ml/matmul_q8.go:93-119). */
+int wg_matmul_test(uint32_t qtype, const void* raw, int rows, int cols,
+                   const float* x, int m, float* out, int path);
+
+/* ---- measurement hooks used by bench.py ---------------------------------- */
+enum { WG_KCLASS_GEMV = 0, WG_KCLASS_SELF_ATTN = 1, WG_KCLASS_CROSS_ATTN = 2, WG_KCLASS_LOGITS = 3 };
+/* Re-launches one kernel class over all layers of one step on the job's own
+ * stream (device 0), iters times, between two CUDA events; *ms = mean time
+ * of one launch, *bytes = algorithmic bytes of one launch. Call after
+ * wg_job_start. */
+int wg_job_time_kernel(wg_job* j, int kclass, int iters, double* ms, double* bytes);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WG_DECODER_H */

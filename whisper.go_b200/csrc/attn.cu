@@ -1,0 +1,495 @@
+// attn.cu — decoder attention over the KV caches.
+//
+// Replaces ml.ScaledDotProductAttentionInto (internal/ml/attention.go:193-317)
+// as called by runDecoderSelfAttn (internal/model/decoder.go:836-908) and
+// runDecoderCrossAttn (:911-971): scores = q.k * 1/sqrt(hd), softmax with the
+// reference fast exponential (fastExpApprox, attention.go:34-61) against the
+// exact row maximum, weights = e * (1/sum), out = weights . V.
+//
+//  attn_simt_kernel: one CTA per (row, head); used for self-attention (one
+//    query row per KV history) and for cross-attention when hd != 64.
+//  cross_attn_mma_kernel: cross-attention where the beams of an utterance
+//    share one K/V read. A thread-block cluster splits the 1500 encoder
+//    frames; the row maximum and the exponential sum are exchanged through
+//    distributed shared memory so the softmax uses the exact global maximum
+//    like the reference; Q.K^T and P.V run on mma.m16n8k16 (f16 in, f32
+//    accumulate).
+#include <cooperative_groups.h>
+
+#include "kernels.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace wg {
+namespace {
+
+// ---------------------------------------------------------------------------
+// SIMT attention
+// ---------------------------------------------------------------------------
+struct SimtArgs {
+  const float* q;
+  int ldq;
+  const __half* kv;
+  int64_t slab_stride;   // elements between KV slabs (rows or utterances)
+  int64_t head_stride;   // elements between heads inside a K (or V) block
+  int64_t v_off;         // K -> V offset inside a slab
+  const int* tbl;        // [R][tbl_ld] slab of each position, or nullptr
+  int tbl_ld;
+  int rows_per_slab;     // slab = r / rows_per_slab when tbl == nullptr
+  int H, hd;
+  int n_mode;            // 0: n = *pos + 1; 1: n = 1; 2: n = n_fixed
+  int n_fixed;
+  const int* pos;
+  int zero_unless_pos0;
+  __half* out16;
+  int ldo;
+};
+
+constexpr int SIMT_WARPS = 4;
+
+__global__ void __launch_bounds__(SIMT_WARPS * 32) attn_simt_kernel(SimtArgs a) {
+  extern __shared__ float sm[];  // scores [n] then reduction scratch
+  const int r = blockIdx.x, h = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hd = a.hd;
+  const int p = (a.n_mode == 0 || a.zero_unless_pos0) ? *a.pos : 0;
+  int n = a.n_mode == 0 ? p + 1 : (a.n_mode == 1 ? 1 : a.n_fixed);
+  __half* out = a.out16 + (int64_t)r * a.ldo + h * hd;
+  if (a.zero_unless_pos0 && p != 0) {
+    // K/V slot 0 was reset to zero (decoder.go:593 -> :372-386): scores are
+    // 0, the single weight is 1 and the output is exactly 0.
+    for (int c = threadIdx.x; c < hd; c += blockDim.x) out[c] = __float2half_rn(0.f);
+    return;
+  }
+  float* scores = sm;
+  float* red = sm + ((n + 3) & ~3);
+  __shared__ float qs[64];
+  const float* qr = a.q + (int64_t)r * a.ldq + h * hd;
+  for (int c = threadIdx.x; c < 64; c += blockDim.x) qs[c] = c < hd ? qr[c] : 0.f;
+  __syncthreads();
+  const float scale = (float)(1.0 / sqrt((double)hd));
+  const int sub = lane >> 3, dl = (lane & 7) * 8;  // 4 positions per warp step, 8 dims per lane
+  auto slab_of = [&](int t) -> int64_t {
+    return a.tbl ? (int64_t)a.tbl[(int64_t)r * a.tbl_ld + t] : (int64_t)(r / a.rows_per_slab);
+  };
+  // scores
+  for (int t0 = warp * 4; t0 < n; t0 += SIMT_WARPS * 4) {
+    int t = t0 + sub;
+    float part = 0.f;
+    if (t < n) {
+      const __half* kr = a.kv + slab_of(t) * a.slab_stride + (int64_t)h * a.head_stride + (int64_t)t * hd;
+      if (hd == 64) {
+        uint4 raw = *reinterpret_cast<const uint4*>(kr + dl);
+        const __half2* k2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          float2 kf = __half22float2(k2[e]);
+          part = fmaf(qs[dl + 2 * e], kf.x, part);
+          part = fmaf(qs[dl + 2 * e + 1], kf.y, part);
+        }
+      } else {
+        for (int e = 0; e < 8; e++) {
+          int c = dl + e;
+          if (c < hd) part = fmaf(qs[c], __half2float(kr[c]), part);
+        }
+      }
+    }
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    part += __shfl_xor_sync(0xffffffffu, part, 2);
+    part += __shfl_xor_sync(0xffffffffu, part, 4);
+    if (t < n && (lane & 7) == 0) scores[t] = __fmul_rn(part, scale);
+  }
+  __syncthreads();
+  // max
+  float m = -INFINITY;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) m = fmaxf(m, scores[t]);
+  m = warp_max(m);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  m = red[0];
+  for (int w = 1; w < SIMT_WARPS; w++) m = fmaxf(m, red[w]);
+  __syncthreads();
+  // exp + sum
+  float s = 0.f;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    float e = ref_fast_exp(__fsub_rn(scores[t], m));
+    scores[t] = e;
+    s += e;
+  }
+  s = warp_sum(s);
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  s = 0.f;
+  for (int w = 0; w < SIMT_WARPS; w++) s += red[w];
+  const float inv = s == 0.f ? 0.f : __fdiv_rn(1.0f, s);
+  const float uni = __fdiv_rn(1.0f, (float)n);
+  for (int t = threadIdx.x; t < n; t += blockDim.x) scores[t] = s == 0.f ? uni : __fmul_rn(scores[t], inv);
+  __syncthreads();
+  // out = weights . V
+  float o[8];
+#pragma unroll
+  for (int e = 0; e < 8; e++) o[e] = 0.f;
+  for (int t0 = warp * 4; t0 < n; t0 += SIMT_WARPS * 4) {
+    int t = t0 + sub;
+    if (t >= n) continue;
+    const float w = scores[t];
+    const __half* vr = a.kv + slab_of(t) * a.slab_stride + a.v_off + (int64_t)h * a.head_stride + (int64_t)t * hd;
+    if (hd == 64) {
+      uint4 raw = *reinterpret_cast<const uint4*>(vr + dl);
+      const __half2* v2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        float2 vf = __half22float2(v2[e]);
+        o[2 * e] = fmaf(w, vf.x, o[2 * e]);
+        o[2 * e + 1] = fmaf(w, vf.y, o[2 * e + 1]);
+      }
+    } else {
+      for (int e = 0; e < 8; e++)
+        if (dl + e < hd) o[e] = fmaf(w, __half2float(vr[dl + e]), o[e]);
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; e++) {
+    o[e] += __shfl_xor_sync(0xffffffffu, o[e], 8);
+    o[e] += __shfl_xor_sync(0xffffffffu, o[e], 16);
+  }
+  float* ored = red + SIMT_WARPS;  // [SIMT_WARPS][64]
+  if (lane < 8)
+#pragma unroll
+    for (int e = 0; e < 8; e++) ored[warp * 64 + dl + e] = o[e];
+  __syncthreads();
+  for (int c = threadIdx.x; c < hd; c += blockDim.x) {
+    float v = ored[c];
+    for (int w = 1; w < SIMT_WARPS; w++) v += ored[w * 64 + c];
+    out[c] = __float2half_rn(v);
+  }
+}
+
+int launch_simt(const SimtArgs& a, int R, int n_max, cudaStream_t st) {
+  size_t smem = (size_t)(((n_max + 3) & ~3) + SIMT_WARPS + SIMT_WARPS * 64) * 4;
+  if (smem > 48 * 1024) {
+    set_error("attention: %d positions exceed the SIMT kernel's shared memory", n_max);
+    return WG_ERR_UNSUPPORTED;
+  }
+  attn_simt_kernel<<<dim3(R, a.H), SIMT_WARPS * 32, smem, st>>>(a);
+  return launch_status("attn_simt");
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core cross-attention with a cluster split over encoder frames
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t* r, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t* r, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void cp_async16(uint32_t s, const void* g, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(g), "r"(src_bytes));
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  uint32_t u;
+  memcpy(&u, &h, 4);
+  return u;
+}
+
+constexpr int XA_MAX_WARPS = 4;
+
+// grid (S, H, U), cluster (S, 1, 1); block = 32 * wpc; each warp owns 64
+// frames of this CTA's chunk of 64 * wpc frames.
+__global__ void __launch_bounds__(XA_MAX_WARPS * 32)
+    cross_attn_mma_kernel(const float* __restrict__ q, const __half* __restrict__ kvc, int U, int B, int H, int T,
+                          int wpc, __half* __restrict__ out16, int ldo) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = (int)cluster.block_rank();
+  const int csize = (int)cluster.num_blocks();
+  const int h = blockIdx.y, u = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+  const int Tc = 64 * wpc;
+  const int t_begin = crank * Tc;
+  const int d = H * 64;
+  unsigned char* ksm = smem;                      // [Tc][64] halves, 16-byte chunks xor-swizzled
+  unsigned char* vsm = smem + (size_t)Tc * 128;   // [Tc][64]
+  float* stats = reinterpret_cast<float*>(smem + (size_t)Tc * 256);  // [2][16] published to the cluster
+  float* wred = stats + 32;                                          // [wpc][16]
+  float* opart = wred + XA_MAX_WARPS * 16;                           // [16][64] CTA partial output
+  const __half* kbase = kvc + ((int64_t)u * 2 * H + h) * (int64_t)T * 64;
+  const __half* vbase = kbase + (int64_t)H * T * 64;
+  const uint32_t ks_addr = (uint32_t)__cvta_generic_to_shared(ksm);
+  const uint32_t vs_addr = (uint32_t)__cvta_generic_to_shared(vsm);
+  // async loads: K chunk (group 0), V chunk (group 1)
+  for (int i = threadIdx.x; i < Tc * 8; i += blockDim.x) {
+    int row = i >> 3, ch = i & 7;
+    int t = t_begin + row;
+    int ok = t < T ? 16 : 0;
+    int tt = t < T ? t : T - 1;
+    cp_async16(ks_addr + row * 128 + ((ch ^ (row & 7)) << 4), kbase + (int64_t)tt * 64 + ch * 8, ok);
+  }
+  asm volatile("cp.async.commit_group;\n" ::);
+  for (int i = threadIdx.x; i < Tc * 8; i += blockDim.x) {
+    int row = i >> 3, ch = i & 7;
+    int t = t_begin + row;
+    int ok = t < T ? 16 : 0;
+    int tt = t < T ? t : T - 1;
+    cp_async16(vs_addr + row * 128 + ((ch ^ (row & 7)) << 4), vbase + (int64_t)tt * 64 + ch * 8, ok);
+  }
+  asm volatile("cp.async.commit_group;\n" ::);
+  // Q fragments (rows = beams of utterance u), scaled by 1/sqrt(64) = 2^-3 (exact)
+  uint32_t qa[4][4];
+  {
+    const int rg = g, rg8 = g + 8;
+    const float* q0 = q + ((int64_t)u * B + rg) * d + h * 64;
+    const float* q1 = q + ((int64_t)u * B + rg8) * d + h * 64;
+#pragma unroll
+    for (int ks = 0; ks < 4; ks++) {
+      int k0 = ks * 16 + 2 * t4;
+      float a0 = rg < B ? q0[k0] * 0.125f : 0.f, a1 = rg < B ? q0[k0 + 1] * 0.125f : 0.f;
+      float a2 = rg8 < B ? q1[k0] * 0.125f : 0.f, a3 = rg8 < B ? q1[k0 + 1] * 0.125f : 0.f;
+      float a4 = rg < B ? q0[k0 + 8] * 0.125f : 0.f, a5 = rg < B ? q0[k0 + 9] * 0.125f : 0.f;
+      float a6 = rg8 < B ? q1[k0 + 8] * 0.125f : 0.f, a7 = rg8 < B ? q1[k0 + 9] * 0.125f : 0.f;
+      qa[ks][0] = pack_h2(a0, a1);
+      qa[ks][1] = pack_h2(a2, a3);
+      qa[ks][2] = pack_h2(a4, a5);
+      qa[ks][3] = pack_h2(a6, a7);
+    }
+  }
+  asm volatile("cp.async.wait_group 1;\n" ::);
+  __syncthreads();
+  // S = Q K^T for this warp's 64 frames: 8 blocks of 8 frames
+  float sacc[8][4];
+#pragma unroll
+  for (int nb = 0; nb < 8; nb++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) sacc[nb][c] = 0.f;
+  const int wrow0 = warp * 64;
+#pragma unroll
+  for (int nb = 0; nb < 8; nb++) {
+#pragma unroll
+    for (int kp = 0; kp < 2; kp++) {  // pairs of k-steps (32 dims)
+      int row = wrow0 + nb * 8 + (lane & 7);
+      int ch = kp * 4 + (lane >> 3);
+      uint32_t b[4];
+      ldsm_x4(b, ks_addr + row * 128 + ((ch ^ (row & 7)) << 4));
+      mma16816(sacc[nb], qa[2 * kp], b[0], b[1]);
+      mma16816(sacc[nb], qa[2 * kp + 1], b[2], b[3]);
+    }
+  }
+  // mask frames past T; row maxima (rows g and g+8)
+  float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+  for (int nb = 0; nb < 8; nb++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      int t = t_begin + wrow0 + nb * 8 + 2 * t4 + (c & 1);
+      if (t >= T) sacc[nb][c] = -INFINITY;
+      if (c < 2) mx0 = fmaxf(mx0, sacc[nb][c]);
+      else mx1 = fmaxf(mx1, sacc[nb][c]);
+    }
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+  if (t4 == 0) {
+    wred[warp * 16 + g] = mx0;
+    wred[warp * 16 + g + 8] = mx1;
+  }
+  __syncthreads();
+  if (threadIdx.x < 16) {
+    float m = wred[threadIdx.x];
+    for (int w = 1; w < wpc; w++) m = fmaxf(m, wred[w * 16 + threadIdx.x]);
+    stats[threadIdx.x] = m;
+  }
+  cluster.sync();
+  float gm0 = -INFINITY, gm1 = -INFINITY;
+  for (int rk = 0; rk < csize; rk++) {
+    const float* rs = cluster.map_shared_rank(stats, rk);
+    gm0 = fmaxf(gm0, rs[g]);
+    gm1 = fmaxf(gm1, rs[g + 8]);
+  }
+  // exponentials against the global maximum; partial sums
+  float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+  for (int nb = 0; nb < 8; nb++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      float e = ref_fast_exp(__fsub_rn(sacc[nb][c], c < 2 ? gm0 : gm1));
+      sacc[nb][c] = e;
+      if (c < 2) sum0 += e;
+      else sum1 += e;
+    }
+  sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
+  sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
+  sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
+  sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
+  __syncthreads();
+  if (t4 == 0) {
+    wred[warp * 16 + g] = sum0;
+    wred[warp * 16 + g + 8] = sum1;
+  }
+  __syncthreads();
+  if (threadIdx.x < 16) {
+    float s = wred[threadIdx.x];
+    for (int w = 1; w < wpc; w++) s += wred[w * 16 + threadIdx.x];
+    stats[16 + threadIdx.x] = s;
+  }
+  cluster.sync();
+  float gs0 = 0.f, gs1 = 0.f;
+  for (int rk = 0; rk < csize; rk++) {
+    const float* rs = cluster.map_shared_rank(stats, rk);
+    gs0 += rs[16 + g];
+    gs1 += rs[16 + g + 8];
+  }
+  const float inv0 = gs0 == 0.f ? 0.f : __fdiv_rn(1.f, gs0);
+  const float inv1 = gs1 == 0.f ? 0.f : __fdiv_rn(1.f, gs1);
+  // weights (e * 1/sum) as f16 A fragments
+  uint32_t pa[4][4];
+#pragma unroll
+  for (int kk = 0; kk < 4; kk++) {
+    pa[kk][0] = pack_h2(__fmul_rn(sacc[2 * kk][0], inv0), __fmul_rn(sacc[2 * kk][1], inv0));
+    pa[kk][1] = pack_h2(__fmul_rn(sacc[2 * kk][2], inv1), __fmul_rn(sacc[2 * kk][3], inv1));
+    pa[kk][2] = pack_h2(__fmul_rn(sacc[2 * kk + 1][0], inv0), __fmul_rn(sacc[2 * kk + 1][1], inv0));
+    pa[kk][3] = pack_h2(__fmul_rn(sacc[2 * kk + 1][2], inv1), __fmul_rn(sacc[2 * kk + 1][3], inv1));
+  }
+  asm volatile("cp.async.wait_group 0;\n" ::);
+  __syncthreads();
+  // O = P V over this warp's 64 frames: 8 blocks of 8 dims
+  float oacc[8][4];
+#pragma unroll
+  for (int nd = 0; nd < 8; nd++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) oacc[nd][c] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < 4; kk++) {
+#pragma unroll
+    for (int ndp = 0; ndp < 4; ndp++) {  // pairs of 8-dim blocks
+      int mtx = lane >> 3;
+      int row = wrow0 + kk * 16 + (mtx & 1) * 8 + (lane & 7);
+      int ch = ndp * 2 + (mtx >> 1);
+      uint32_t b[4];
+      ldsm_x4_t(b, vs_addr + row * 128 + ((ch ^ (row & 7)) << 4));
+      mma16816(oacc[2 * ndp], pa[kk], b[0], b[1]);
+      mma16816(oacc[2 * ndp + 1], pa[kk], b[2], b[3]);
+    }
+  }
+  // CTA partial: warps in order
+  for (int w = 0; w < wpc; w++) {
+    if (warp == w) {
+#pragma unroll
+      for (int nd = 0; nd < 8; nd++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          int row = g + ((c >> 1) << 3), col = nd * 8 + 2 * t4 + (c & 1);
+          float* dst = opart + row * 64 + col;
+          *dst = (w == 0) ? oacc[nd][c] : *dst + oacc[nd][c];
+        }
+    }
+    __syncthreads();
+  }
+  cluster.sync();
+  if (crank == 0) {
+    for (int i = threadIdx.x; i < B * 64; i += blockDim.x) {
+      int row = i >> 6, col = i & 63;
+      float v = 0.f;
+      for (int rk = 0; rk < csize; rk++) v += cluster.map_shared_rank(opart, rk)[row * 64 + col];
+      out16[((int64_t)u * B + row) * ldo + h * 64 + col] = __float2half_rn(v);
+    }
+  }
+  cluster.sync();
+}
+
+}  // namespace
+
+int launch_self_attn(const SelfAttnArgs& s, cudaStream_t st) {
+  SimtArgs a{};
+  a.q = s.q;
+  a.ldq = s.H * s.hd;
+  a.kv = s.kv;
+  a.slab_stride = (int64_t)2 * s.H * s.Tmax * s.hd;
+  a.head_stride = (int64_t)s.Tmax * s.hd;
+  a.v_off = (int64_t)s.H * s.Tmax * s.hd;
+  a.tbl = s.ref_compat ? nullptr : s.tbl;
+  a.tbl_ld = s.Tmax;
+  a.rows_per_slab = 1;
+  a.H = s.H;
+  a.hd = s.hd;
+  a.n_mode = s.ref_compat ? 1 : 0;
+  a.pos = s.pos;
+  a.zero_unless_pos0 = s.zero_unless_pos0;
+  a.out16 = s.out16;
+  a.ldo = (s.H * s.hd + 7) / 8 * 8;
+  return launch_simt(a, s.R, s.Tmax, st);
+}
+
+static int cross_wpc(int T) {
+  int w = (T + 511) / 512;
+  return w < 1 ? 1 : w;
+}
+
+int init_attn_attributes() {
+  cudaError_t e = cudaFuncSetAttribute(cross_attn_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       XA_MAX_WARPS * 64 * 256 + (32 + XA_MAX_WARPS * 16 + 16 * 64) * 4);
+  if (e != cudaSuccess) {
+    set_error("cudaFuncSetAttribute(cross_attn): %s", cudaGetErrorString(e));
+    return WG_ERR_CUDA;
+  }
+  return WG_OK;
+}
+
+int launch_cross_attn(const CrossAttnArgs& c, cudaStream_t st) {
+  const int ldo = (c.H * c.hd + 7) / 8 * 8;
+  int wpc = cross_wpc(c.T);
+  if (c.hd != 64 || c.B > 16 || wpc > XA_MAX_WARPS) {
+    SimtArgs a{};
+    a.q = c.q;
+    a.ldq = c.H * c.hd;
+    a.kv = c.kv;
+    a.slab_stride = (int64_t)2 * c.H * c.T * c.hd;
+    a.head_stride = (int64_t)c.T * c.hd;
+    a.v_off = (int64_t)c.H * c.T * c.hd;
+    a.tbl = nullptr;
+    a.rows_per_slab = c.B;
+    a.H = c.H;
+    a.hd = c.hd;
+    a.n_mode = 2;
+    a.n_fixed = c.T;
+    a.pos = nullptr;  // not read in n_mode 2
+    a.out16 = c.out16;
+    a.ldo = ldo;
+    return launch_simt(a, c.U * c.B, c.T, st);
+  }
+  int S = (c.T + 64 * wpc - 1) / (64 * wpc);
+  size_t smem = (size_t)wpc * 64 * 256 + (32 + XA_MAX_WARPS * 16 + 16 * 64) * 4;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(S, c.H, c.U);
+  cfg.blockDim = dim3(32 * wpc, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, cross_attn_mma_kernel, c.q, c.kv, c.U, c.B, c.H, c.T, wpc, c.out16, ldo);
+  if (e != cudaSuccess) {
+    set_error("launch of cross_attn_mma failed: %s", cudaGetErrorString(e));
+    return WG_ERR_CUDA;
+  }
+  return launch_status("cross_attn_mma");
+}
+
+}  // namespace wg

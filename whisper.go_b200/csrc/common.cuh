@@ -1,0 +1,138 @@
+// common.cuh — shared definitions of the B200 decoder library (sm_100a).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <cstdio>
+
+#include "../../include/wg_decoder.h"
+
+namespace wg {
+
+// ---- host-side errors ------------------------------------------------------
+void set_error(const char* fmt, ...) __attribute__((format(printf, 1, 2)));
+const char* last_error();
+
+#define WG_CHECK_CUDA(call)                                                                  \
+  do {                                                                                       \
+    cudaError_t e_ = (call);                                                                 \
+    if (e_ != cudaSuccess) {                                                                 \
+      ::wg::set_error("%s:%d: %s failed: %s", __FILE__, __LINE__, #call, cudaGetErrorString(e_)); \
+      return e_ == cudaErrorMemoryAllocation ? WG_ERR_OOM : WG_ERR_CUDA;                     \
+    }                                                                                        \
+  } while (0)
+
+#define WG_CHECK(expr)        \
+  do {                        \
+    int rc_ = (expr);         \
+    if (rc_ != WG_OK) return rc_; \
+  } while (0)
+
+// Count of our own kernel launches (wg_kernel_launch_count). Graph replays
+// add the number of kernel nodes of the graph.
+extern std::atomic<int64_t> g_launches;
+inline void count_launch(int64_t n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+// Checks the launch that was just enqueued.
+inline int launch_status(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("launch of %s failed: %s", what, cudaGetErrorString(e));
+    return WG_ERR_CUDA;
+  }
+  count_launch();
+  return WG_OK;
+}
+
+// ---- device weight layout ----------------------------------------------------
+//
+// Quantised matrices [rows, cols] (cols % 32 == 0) are repacked at upload into
+// the "tile16" layout consumed by the tensor-core GEMV/GEMM: rows are grouped
+// in tiles of 16, columns in quant blocks of 32, and for every (tile, block)
+// each of the 32 lanes of a warp owns a contiguous payload that is exactly its
+// A-fragment of two mma.m16n8k16 steps (rows g and g+8, k = 2t,2t+1,2t+8,2t+9
+// and +16; g = lane/4, t = lane%4):
+//   qs : [NT][KB][32][PB] bytes, PB = 16 (Q8_0: int8 codes) or 8 (4/5-bit:
+//        nibble pairs, pair p of step s at bits 4p and 16+4p of word s)
+//   dsc: [NT][KB][8] half2 = (d[row g], d[row g+8])     (all quant types)
+//   msc: [NT][KB][8] half2 = (m[row g], m[row g+8])     (Q4_1, Q5_1)
+//   hb : [NT][KB][32] u16 lane payload of 5th bits      (Q5_0, Q5_1)
+// Byte count equals the GGUF block bytes (plus the row padding to 16).
+// F32 / F16 matrices stay dense row-major in qs.
+struct DMat {
+  uint32_t qtype = 0;
+  int rows = 0, cols = 0;
+  int ntiles = 0, kblocks = 0;
+  uint8_t* qs = nullptr;
+  __half2* dsc = nullptr;
+  __half2* msc = nullptr;
+  uint16_t* hb = nullptr;
+};
+
+__host__ __device__ inline bool qtype_is_quant(uint32_t q) {
+  return q == WG_QTYPE_Q4_0 || q == WG_QTYPE_Q4_1 || q == WG_QTYPE_Q5_0 || q == WG_QTYPE_Q5_1 ||
+         q == WG_QTYPE_Q8_0;
+}
+__host__ __device__ inline int qtype_payload_bytes(uint32_t q) { return q == WG_QTYPE_Q8_0 ? 16 : 8; }
+__host__ __device__ inline bool qtype_has_min(uint32_t q) { return q == WG_QTYPE_Q4_1 || q == WG_QTYPE_Q5_1; }
+__host__ __device__ inline bool qtype_has_hbits(uint32_t q) { return q == WG_QTYPE_Q5_0 || q == WG_QTYPE_Q5_1; }
+__host__ __device__ inline int64_t gguf_block_bytes(uint32_t q) {
+  switch (q) {
+    case WG_QTYPE_Q4_0: return 18;
+    case WG_QTYPE_Q4_1: return 20;
+    case WG_QTYPE_Q5_0: return 22;
+    case WG_QTYPE_Q5_1: return 24;
+    case WG_QTYPE_Q8_0: return 34;
+    default: return 0;
+  }
+}
+inline int64_t gguf_row_bytes(uint32_t q, int64_t cols) {
+  if (q == WG_QTYPE_F32) return cols * 4;
+  if (q == WG_QTYPE_F16) return cols * 2;
+  int64_t bb = gguf_block_bytes(q);
+  return bb ? ((cols + 31) / 32) * bb : -1;
+}
+
+// ---- device helpers -------------------------------------------------------------
+
+// IEEE half -> float (exact), for raw GGUF f16 fields.
+__device__ __forceinline__ float h2f_bits(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+// The reference softmax exponential, internal/ml/attention.go:34-61
+// (fastExpApprox): k = floor(x/ln2), r = x - k*ln2, 4th-order Taylor
+// polynomial of exp(r) times 2^k, 0 for x <= -20. Every product and sum is
+// rounded separately, as Go evaluates it.
+__device__ __forceinline__ float ref_fast_exp(float x) {
+  const float invLn2 = 1.4426950408889634f;
+  const float ln2 = 0.6931471805599453f;
+  if (x <= -20.0f) return 0.0f;
+  float y = __fmul_rn(x, invLn2);
+  int k = (int)y;
+  if ((float)k > y) k--;
+  float r = __fsub_rn(x, __fmul_rn((float)k, ln2));
+  float r2 = __fmul_rn(r, r);
+  float r3 = __fmul_rn(r2, r);
+  float r4 = __fmul_rn(r3, r);
+  float poly = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(1.0f, r), __fmul_rn(0.5f, r2)),
+                                   __fmul_rn((float)(1.0 / 6.0), r3)),
+                         __fmul_rn((float)(1.0 / 24.0), r4));
+  if (k < -126) return 0.0f;
+  if (k > 127) return 3.40282346638528859811704183484516925440e+38f;
+  return __fmul_rn(poly, __uint_as_float((uint32_t)(k + 127) << 23));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+}  // namespace wg

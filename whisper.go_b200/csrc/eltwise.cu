@@ -1,0 +1,104 @@
+// eltwise.cu — embedding gather and LayerNorm of the decoder token loop.
+#include "kernels.cuh"
+
+namespace wg {
+namespace {
+
+// Exact fp32 dequantisation of element (r, k) of a device matrix
+// (internal/gguf/dequant.go:92-201 through the tile16 layout).
+__device__ __forceinline__ float dmat_elem(const DMat& m, int r, int k) {
+  if (m.qtype == WG_QTYPE_F32) return reinterpret_cast<const float*>(m.qs)[(int64_t)r * m.cols + k];
+  if (m.qtype == WG_QTYPE_F16) return __half2float(reinterpret_cast<const __half*>(m.qs)[(int64_t)r * m.cols + k]);
+  int tile = r >> 4, gg = r & 15, g = gg & 7, hi = gg >> 3;
+  int kb = k >> 5, kk = k & 31, s = kk >> 4, kr = kk & 15;
+  int t = (kr & 7) >> 1, e = kr & 1, reg = ((kr >> 3) << 1) | hi;
+  int lane = g * 4 + t;
+  int64_t slot = (int64_t)tile * m.kblocks + kb;
+  __half2 dd = m.dsc[slot * 8 + g];
+  float d = __half2float(hi ? __high2half(dd) : __low2half(dd));
+  if (m.qtype == WG_QTYPE_Q8_0) {
+    int8_t q = (int8_t)m.qs[(slot * 32 + lane) * 16 + s * 8 + reg * 2 + e];
+    return __fmul_rn(d, (float)q);
+  }
+  uint2 w2 = reinterpret_cast<const uint2*>(m.qs)[slot * 32 + lane];
+  uint32_t w = s ? w2.y : w2.x;
+  uint32_t q = (w >> (e ? 16 + 4 * reg : 4 * reg)) & 0xF;
+  if (m.hb) q |= (((uint32_t)m.hb[slot * 32 + lane] >> (2 * (4 * s + reg) + e)) & 1u) << 4;
+  if (m.qtype == WG_QTYPE_Q4_0) return __fmul_rn(d, (float)((int)q - 8));
+  if (m.qtype == WG_QTYPE_Q5_0) return __fmul_rn(d, (float)((int)q - 16));
+  __half2 mm = m.msc[slot * 8 + g];
+  float mn = __half2float(hi ? __high2half(mm) : __low2half(mm));
+  return __fadd_rn(__fmul_rn(d, (float)q), mn);
+}
+
+// x[r] = tokEmb[tok[r]] + posEmb[pos] (decoder.go:756-773). The embedding row
+// is read from the quantised matrix (the reference reads only the dense
+// tensor, which is empty when the embedding is quantised, decoder.go:761-766).
+__global__ void embed_kernel(DMat te, const float* __restrict__ pos_emb, const int* __restrict__ tokens,
+                             const int* __restrict__ pos, int pos_offset, int d, float* __restrict__ x) {
+  int r = blockIdx.x;
+  int tok = tokens[r];
+  int p = *pos + pos_offset;
+  if (tok < 0 || tok >= te.rows) tok = 0;  // guarded: ids are validated on the host
+  for (int i = threadIdx.x; i < d; i += blockDim.x)
+    x[(int64_t)r * d + i] = __fadd_rn(dmat_elem(te, tok, i), pos_emb[(int64_t)p * d + i]);
+}
+
+// internal/ml/ops.go:153-202 (LayerNormInto): two-pass mean / variance in
+// fp32, std = float32(sqrt(float64(var + eps))) (== IEEE sqrtf),
+// out = w*(v-mean)/std + b. One warp per row.
+__global__ void layernorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                 const float* __restrict__ b, int R, int d, __half* __restrict__ out16,
+                                 int ld16, float* __restrict__ out32) {
+  int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  int lane = threadIdx.x & 31;
+  if (r >= R) return;
+  const float* xr = x + (int64_t)r * d;
+  float s = 0.f;
+  for (int i = lane; i < d; i += 32) s += xr[i];
+  s = warp_sum(s);
+  float mean = __fdiv_rn(s, (float)d);
+  float v = 0.f;
+  for (int i = lane; i < d; i += 32) {
+    float dd = __fsub_rn(xr[i], mean);
+    v = __fmaf_rn(dd, dd, v);
+  }
+  v = warp_sum(v);
+  float var = __fdiv_rn(v, (float)d);
+  float sd = __fsqrt_rn(__fadd_rn(var, 1e-5f));
+  for (int i = lane; i < d; i += 32) {
+    float o = __fadd_rn(__fdiv_rn(__fmul_rn(w[i], __fsub_rn(xr[i], mean)), sd), b[i]);
+    if (out16) out16[(int64_t)r * ld16 + i] = __float2half_rn(o);
+    if (out32) out32[(int64_t)r * d + i] = o;
+  }
+}
+
+__global__ void f32_to_f16_kernel(const float* __restrict__ in, __half* __restrict__ out, int64_t n) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) out[i] = __float2half_rn(in[i]);
+}
+
+}  // namespace
+
+int launch_embed(const DMat& te, const float* pos_emb, const int* tokens, const int* pos, int pos_offset, int R,
+                 int d, float* x, cudaStream_t st) {
+  embed_kernel<<<R, 256, 0, st>>>(te, pos_emb, tokens, pos, pos_offset, d, x);
+  return launch_status("embed");
+}
+
+int launch_layernorm(const float* x, const float* w, const float* b, int R, int d, __half* out16, float* out32,
+                     cudaStream_t st) {
+  int ld16 = (d + 7) / 8 * 8;
+  layernorm_kernel<<<(R + 7) / 8, 256, 0, st>>>(x, w, b, R, d, out16, ld16, out32);
+  return launch_status("layernorm");
+}
+
+int launch_f32_to_f16(const float* in, __half* out, int64_t n, cudaStream_t st) {
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  f32_to_f16_kernel<<<(unsigned)blocks, 256, 0, st>>>(in, out, n);
+  return launch_status("f32_to_f16");
+}
+
+}  // namespace wg

@@ -1,0 +1,414 @@
+// gemm.cu — fused dequant GEMV / GEMM: out[r, n] = sum_k X[r, k] * deq(W[n, k]).
+//
+// Replaces ml.MatMulQuantTransBInto (internal/ml/matmul_q8.go:93-119) and
+// its per-type dot kernels (:237-429, the AVX2 routines of
+// matmul_q8_kernels_amd64.go and dot_int8_f32_avx2_amd64.s) on the decoder
+// token loop, with the bias / residual / GELU / KV-cache writes of
+// internal/model/decoder.go fused into the epilogue.
+//
+// Weights stream from HBM in the tile16 layout (one coalesced 16- or 8-byte
+// load per lane per 16x32 tile-block), are dequantised in registers straight
+// into mma.m16n8k16 A fragments (f16 = d*q rounded once; f32 accumulation),
+// and multiply activation rows staged in shared memory as f16 B fragments.
+//   small-R kernel (R <= 16): one 16-row tile per CTA, 8 warps split K,
+//     whole activation block resident in shared memory, deterministic
+//     shared-memory reduction across warps.
+//   large-R kernel (R > 16): 64 weight rows x 64 activation rows per CTA,
+//     activation K-slices through a 4-stage cp.async ring.
+#include "kernels.cuh"
+
+namespace wg {
+namespace {
+
+__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 ldg_stream16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint2 ldg_stream8(const void* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
+  uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+__device__ __forceinline__ uint32_t h2_as_u32(__half2 h) {
+  uint32_t u;
+  memcpy(&u, &h, 4);
+  return u;
+}
+__device__ __forceinline__ __half2 u32_as_h2(uint32_t u) {
+  __half2 h;
+  memcpy(&h, &u, 4);
+  return h;
+}
+
+// One lane's share of one (tile, block).
+struct Pay {
+  uint4 q;
+  uint32_t hb;
+  __half2 d, m;
+};
+
+template <uint32_t QT>
+__device__ __forceinline__ Pay load_payload(const DMat& W, int64_t slot, int lane) {
+  Pay p;
+  if (QT == WG_QTYPE_Q8_0) {
+    p.q = ldg_stream16(W.qs + (slot * 32 + lane) * 16);
+  } else {
+    uint2 v = ldg_stream8(W.qs + (slot * 32 + lane) * 8);
+    p.q = make_uint4(v.x, v.y, 0, 0);
+  }
+  p.d = W.dsc[slot * 8 + (lane >> 2)];
+  if (QT == WG_QTYPE_Q4_1 || QT == WG_QTYPE_Q5_1) p.m = W.msc[slot * 8 + (lane >> 2)];
+  else p.m = __float2half2_rn(0.f);
+  if (QT == WG_QTYPE_Q5_0 || QT == WG_QTYPE_Q5_1) p.hb = W.hb[slot * 32 + lane];
+  else p.hb = 0;
+  return p;
+}
+
+// A fragment of mma step s (0/1) of a 32-wide quant block.
+// reg 0: row g, k 2t..2t+1; reg 1: row g+8; reg 2: row g, k+8; reg 3: row g+8, k+8.
+template <uint32_t QT>
+__device__ __forceinline__ void dequant_step(const Pay& p, int s, uint32_t* a) {
+  const __half2 dg = __low2half2(p.d), dg8 = __high2half2(p.d);
+  if (QT == WG_QTYPE_Q8_0) {
+    uint32_t w0 = (s ? p.q.z : p.q.x) ^ 0x80808080u;
+    uint32_t w1 = (s ? p.q.w : p.q.y) ^ 0x80808080u;
+    const __half2 bias = __float2half2_rn(1152.f);  // 1024 + 128
+    __half2 h0 = __hsub2(u32_as_h2(__byte_perm(w0, 0x64, 0x4140)), bias);
+    __half2 h1 = __hsub2(u32_as_h2(__byte_perm(w0, 0x64, 0x4342)), bias);
+    __half2 h2 = __hsub2(u32_as_h2(__byte_perm(w1, 0x64, 0x4140)), bias);
+    __half2 h3 = __hsub2(u32_as_h2(__byte_perm(w1, 0x64, 0x4342)), bias);
+    a[0] = h2_as_u32(__hmul2(h0, dg));
+    a[1] = h2_as_u32(__hmul2(h1, dg8));
+    a[2] = h2_as_u32(__hmul2(h2, dg));
+    a[3] = h2_as_u32(__hmul2(h3, dg8));
+  } else {
+    uint32_t w = s ? p.q.y : p.q.x;
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      uint32_t hq = ((w >> (4 * r)) & 0x000F000Fu) | 0x64006400u;
+      if (QT == WG_QTYPE_Q5_0 || QT == WG_QTYPE_Q5_1) {
+        uint32_t b = (p.hb >> (2 * (4 * s + r))) & 3u;
+        hq |= ((b & 1u) << 4) | ((b >> 1) << 20);
+      }
+      const __half2 d = (r & 1) ? dg8 : dg;
+      __half2 v;
+      if (QT == WG_QTYPE_Q4_0) v = __hmul2(__hsub2(u32_as_h2(hq), __float2half2_rn(1032.f)), d);
+      else if (QT == WG_QTYPE_Q5_0) v = __hmul2(__hsub2(u32_as_h2(hq), __float2half2_rn(1040.f)), d);
+      else {
+        const __half2 m = (r & 1) ? __high2half2(p.m) : __low2half2(p.m);
+        v = __hfma2(__hsub2(u32_as_h2(hq), __float2half2_rn(1024.f)), d, m);
+      }
+      a[r] = h2_as_u32(v);
+    }
+  }
+}
+
+// GELU of internal/ml/ops.go:102-122 (tanh form, tanh in float64).
+__device__ __forceinline__ float ref_gelu(float x) {
+  const float s2p = 0.7978845608028654f, c = 0.044715f;
+  float inner = __fmul_rn(s2p, __fadd_rn(x, __fmul_rn(__fmul_rn(__fmul_rn(c, x), x), x)));
+  float th = (float)(1.0 + tanh((double)inner));
+  return __fmul_rn(__fmul_rn(x, 0.5f), th);
+}
+
+__device__ __forceinline__ void epi_store(const Epi& e, int r, int n, float v) {
+  switch (e.mode) {
+    case EPI_F32:
+      if (e.bias) v = __fadd_rn(v, e.bias[n]);
+      e.out[(int64_t)r * e.ldo + n] = v;
+      break;
+    case EPI_RESID: {
+      float* p = e.out + (int64_t)r * e.ldo + n;
+      *p = __fadd_rn(*p, __fadd_rn(v, e.bias ? e.bias[n] : 0.f));
+      break;
+    }
+    case EPI_GELU_F16:
+      if (e.bias) v = __fadd_rn(v, e.bias[n]);
+      e.out16[(int64_t)r * e.ldo + n] = __float2half_rn(ref_gelu(v));
+      break;
+    case EPI_QKV: {
+      int seg = n / e.d, j = n - seg * e.d, h = j / e.hd, c = j - h * e.hd;
+      if (seg == 0) {
+        e.out[(int64_t)r * e.ldo + j] = __fadd_rn(v, e.bias_q[j]);
+      } else {
+        if (seg == 2) v = __fadd_rn(v, e.bias_v[j]);
+        int p = *e.pos;
+        e.kv[((((int64_t)r * 2 + (seg - 1)) * e.H + h) * e.T + p) * e.hd + c] = __float2half_rn(v);
+      }
+      break;
+    }
+    case EPI_CROSS_KV: {
+      int u = r / e.T, tt = r - u * e.T;
+      int lk = n / e.d, j = n - lk * e.d, l = lk >> 1, kv = lk & 1, h = j / e.hd, c = j - h * e.hd;
+      if (kv) v = __fadd_rn(v, e.bias_v[(int64_t)l * e.d + j]);
+      e.kv[(((((int64_t)l * e.U + u) * 2 + kv) * e.H + h) * e.T + tt) * e.hd + c] = __float2half_rn(v);
+      break;
+    }
+  }
+}
+
+// ---- small-R kernel ------------------------------------------------------------------
+constexpr int SMALL_WK = 8;  // warps splitting K
+constexpr int SMALL_PF = 4;  // blocks in flight per warp
+
+template <uint32_t QT, int NB>
+__global__ void __launch_bounds__(SMALL_WK * 32)
+    gemv_small_kernel(DMat W, const __half* __restrict__ X, int ldx, Epi e) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  constexpr int RC = NB * 8;
+  const int K = W.cols, KB = W.kblocks;
+  const int xs = K + 8;  // padded row stride in halves: conflict-free B-fragment loads
+  __half* xsm = reinterpret_cast<__half*>(smem);
+  const int tile = blockIdx.x;
+  const int r0 = blockIdx.y * RC;
+  const int cpr = K / 8;
+  for (int i = threadIdx.x; i < RC * cpr; i += blockDim.x) {
+    int rr = i / cpr, cc = i - rr * cpr;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r0 + rr < e.R) v = *reinterpret_cast<const uint4*>(X + (int64_t)(r0 + rr) * ldx + cc * 8);
+    *reinterpret_cast<uint4*>(xsm + rr * xs + cc * 8) = v;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  float acc[NB][4];
+#pragma unroll
+  for (int nb = 0; nb < NB; nb++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) acc[nb][c] = 0.f;
+  const int64_t slot0 = (int64_t)tile * KB;
+  for (int j0 = 0;; j0 += SMALL_PF) {
+    const int kbase = warp + SMALL_WK * j0;
+    if (kbase >= KB) break;
+    Pay p[SMALL_PF];
+#pragma unroll
+    for (int i = 0; i < SMALL_PF; i++) {
+      int kb = kbase + SMALL_WK * i;
+      if (kb < KB) p[i] = load_payload<QT>(W, slot0 + kb, lane);
+    }
+#pragma unroll
+    for (int i = 0; i < SMALL_PF; i++) {
+      int kb = kbase + SMALL_WK * i;
+      if (kb < KB) {
+#pragma unroll
+        for (int s = 0; s < 2; s++) {
+          uint32_t a[4];
+          dequant_step<QT>(p[i], s, a);
+          const int k0 = kb * 32 + s * 16 + 2 * t;
+#pragma unroll
+          for (int nb = 0; nb < NB; nb++) {
+            const __half* xr = xsm + (nb * 8 + g) * xs + k0;
+            uint32_t b0 = *reinterpret_cast<const uint32_t*>(xr);
+            uint32_t b1 = *reinterpret_cast<const uint32_t*>(xr + 8);
+            mma16816(acc[nb], a, b0, b1);
+          }
+        }
+      }
+    }
+  }
+  float* red = reinterpret_cast<float*>(smem + (size_t)RC * xs * 2);
+#pragma unroll
+  for (int nb = 0; nb < NB; nb++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) red[((warp * NB + nb) * 4 + c) * 32 + lane] = acc[nb][c];
+  __syncthreads();
+  if (warp != 0) return;
+#pragma unroll
+  for (int nb = 0; nb < NB; nb++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      float v = acc[nb][c];
+      for (int w = 1; w < SMALL_WK; w++) v += red[((w * NB + nb) * 4 + c) * 32 + lane];
+      int n = tile * 16 + g + ((c >> 1) << 3);
+      int r = r0 + nb * 8 + 2 * t + (c & 1);
+      if (n < e.N && r < e.R) epi_store(e, r, n, v);
+    }
+}
+
+// ---- large-R kernel ------------------------------------------------------------------
+constexpr int LG_RC = 64, LG_NB = 8, LG_STAGES = 4, LG_XS = 40;
+
+template <uint32_t QT>
+__global__ void __launch_bounds__(128) gemm_large_kernel(DMat W, const __half* __restrict__ X, int ldx, Epi e) {
+  __shared__ __align__(16) __half xs[LG_STAGES][LG_RC * LG_XS];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int tile = blockIdx.x * 4 + warp;
+  const bool tile_ok = tile < W.ntiles;
+  const int r0 = blockIdx.y * LG_RC;
+  const int KB = W.kblocks;
+  auto load_stage = [&](int kb, int stg) {
+#pragma unroll
+    for (int c = threadIdx.x; c < LG_RC * 4; c += 128) {
+      int rr = c >> 2, cc = c & 3;
+      int r = r0 + rr;
+      const __half* src = X + (int64_t)(r < e.R ? r : e.R - 1) * ldx + kb * 32 + cc * 8;
+      cp_async16(&xs[stg][rr * LG_XS + cc * 8], src, r < e.R ? 16 : 0);
+    }
+  };
+#pragma unroll
+  for (int s = 0; s < LG_STAGES - 1; s++) {
+    if (s < KB) load_stage(s, s);
+    cp_async_commit();
+  }
+  float acc[LG_NB][4];
+#pragma unroll
+  for (int nb = 0; nb < LG_NB; nb++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) acc[nb][c] = 0.f;
+  const int64_t slot0 = (int64_t)(tile_ok ? tile : 0) * KB;
+  Pay pcur = load_payload<QT>(W, slot0, lane);
+  for (int kb = 0; kb < KB; kb++) {
+    cp_async_wait<LG_STAGES - 2>();
+    __syncthreads();
+    const int nk = kb + LG_STAGES - 1;
+    if (nk < KB) load_stage(nk, nk % LG_STAGES);
+    cp_async_commit();
+    Pay pnext = pcur;
+    if (kb + 1 < KB) pnext = load_payload<QT>(W, slot0 + kb + 1, lane);
+    const __half* xb = xs[kb % LG_STAGES];
+#pragma unroll
+    for (int s = 0; s < 2; s++) {
+      uint32_t a[4];
+      dequant_step<QT>(pcur, s, a);
+#pragma unroll
+      for (int nb = 0; nb < LG_NB; nb++) {
+        const __half* xr = xb + (nb * 8 + g) * LG_XS + s * 16 + 2 * t;
+        uint32_t b0 = *reinterpret_cast<const uint32_t*>(xr);
+        uint32_t b1 = *reinterpret_cast<const uint32_t*>(xr + 8);
+        mma16816(acc[nb], a, b0, b1);
+      }
+    }
+    pcur = pnext;
+  }
+  cp_async_wait<0>();
+  if (!tile_ok) return;
+#pragma unroll
+  for (int nb = 0; nb < LG_NB; nb++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      int n = tile * 16 + g + ((c >> 1) << 3);
+      int r = r0 + nb * 8 + 2 * t + (c & 1);
+      if (n < e.N && r < e.R) epi_store(e, r, n, acc[nb][c]);
+    }
+}
+
+// ---- dense F32 / F16 weights (test-sized models; any K) ----------------------
+template <typename WT>
+__global__ void __launch_bounds__(256) gemv_dense_kernel(const WT* __restrict__ W, int N, int K,
+                                                          const __half* __restrict__ X, int ldx, Epi e) {
+  int n = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (n >= N) return;
+  const WT* w = W + (int64_t)n * K;
+  for (int r = 0; r < e.R; r++) {
+    const __half* x = X + (int64_t)r * ldx;
+    float acc = 0.f;
+    for (int k = lane; k < K; k += 32) acc += (float)w[k] * __half2float(x[k]);
+    acc = warp_sum(acc);
+    if (lane == 0) epi_store(e, r, n, acc);
+  }
+}
+
+template <uint32_t QT, int NB>
+int configure_small_t() {
+  cudaError_t e = cudaFuncSetAttribute(gemv_small_kernel<QT, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       227 * 1024);
+  if (e != cudaSuccess) {
+    set_error("cudaFuncSetAttribute(gemv_small): %s", cudaGetErrorString(e));
+    return WG_ERR_CUDA;
+  }
+  return WG_OK;
+}
+
+template <uint32_t QT, int NB>
+int launch_small_t(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st) {
+  constexpr int RC = NB * 8;
+  size_t smem = (size_t)RC * (W.cols + 8) * 2 + (size_t)SMALL_WK * NB * 4 * 32 * 4;
+  if (smem > 227 * 1024) {
+    set_error("gemv: K=%d too large for the small-R kernel", W.cols);
+    return WG_ERR_UNSUPPORTED;
+  }
+  dim3 grid(W.ntiles, (R + RC - 1) / RC);
+  gemv_small_kernel<QT, NB><<<grid, SMALL_WK * 32, smem, st>>>(W, X, ldx, e);
+  return launch_status("gemv_small");
+}
+
+template <uint32_t QT>
+int launch_q(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st, int path) {
+  if (path == 0) path = R <= 16 ? 1 : 2;
+  if (path == 1) {
+    if (R <= 8) return launch_small_t<QT, 1>(W, X, ldx, R, e, st);
+    if (R <= 16) return launch_small_t<QT, 2>(W, X, ldx, R, e, st);
+    // small kernel in chunks of 16 rows
+    return launch_small_t<QT, 2>(W, X, ldx, R, e, st);
+  }
+  dim3 grid((W.ntiles + 3) / 4, (R + LG_RC - 1) / LG_RC);
+  gemm_large_kernel<QT><<<grid, 128, 0, st>>>(W, X, ldx, e);
+  return launch_status("gemm_large");
+}
+
+}  // namespace
+
+// Opt the small-R kernels into the full 227 KB of shared memory on the
+// current device (called once per device at model creation).
+int init_gemm_attributes() {
+  int rc = WG_OK;
+#define WG_CFG(QT)                                             \
+  if (rc == WG_OK) rc = configure_small_t<QT, 1>();            \
+  if (rc == WG_OK) rc = configure_small_t<QT, 2>();
+  WG_CFG(WG_QTYPE_Q8_0)
+  WG_CFG(WG_QTYPE_Q4_0)
+  WG_CFG(WG_QTYPE_Q4_1)
+  WG_CFG(WG_QTYPE_Q5_0)
+  WG_CFG(WG_QTYPE_Q5_1)
+#undef WG_CFG
+  return rc;
+}
+
+int launch_matmul(const DMat& W, const __half* X, int ldx, int R, const Epi& e_in, cudaStream_t st, int path) {
+  if (R <= 0) return WG_OK;
+  Epi e = e_in;
+  e.R = R;
+  if (e.N <= 0) e.N = W.rows;
+  if (qtype_is_quant(W.qtype) && (ldx % 8 || (reinterpret_cast<uintptr_t>(X) & 15))) {
+    set_error("launch_matmul: activations must be 16-byte aligned rows");
+    return WG_ERR_INVALID;
+  }
+  switch (W.qtype) {
+    case WG_QTYPE_Q8_0: return launch_q<WG_QTYPE_Q8_0>(W, X, ldx, R, e, st, path);
+    case WG_QTYPE_Q4_0: return launch_q<WG_QTYPE_Q4_0>(W, X, ldx, R, e, st, path);
+    case WG_QTYPE_Q4_1: return launch_q<WG_QTYPE_Q4_1>(W, X, ldx, R, e, st, path);
+    case WG_QTYPE_Q5_0: return launch_q<WG_QTYPE_Q5_0>(W, X, ldx, R, e, st, path);
+    case WG_QTYPE_Q5_1: return launch_q<WG_QTYPE_Q5_1>(W, X, ldx, R, e, st, path);
+    case WG_QTYPE_F32:
+      gemv_dense_kernel<float><<<(W.rows + 7) / 8, 256, 0, st>>>(reinterpret_cast<const float*>(W.qs), W.rows,
+                                                                  W.cols, X, ldx, e);
+      return launch_status("gemv_dense_f32");
+    case WG_QTYPE_F16:
+      gemv_dense_kernel<__half><<<(W.rows + 7) / 8, 256, 0, st>>>(reinterpret_cast<const __half*>(W.qs), W.rows,
+                                                                   W.cols, X, ldx, e);
+      return launch_status("gemv_dense_f16");
+    default:
+      set_error("launch_matmul: unsupported tensor type %u", W.qtype);
+      return WG_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace wg

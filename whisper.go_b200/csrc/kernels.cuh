@@ -1,0 +1,120 @@
+// kernels.cuh — launch interfaces of the decoder kernels (one per reference
+// function on the token loop) shared by the C-ABI driver.
+#pragma once
+
+#include "common.cuh"
+
+namespace wg {
+
+// ---- weights (weights.cu) ---------------------------------------------------
+int upload_matrix(const wg_matrix* const* parts, int nparts, DMat* out, cudaStream_t st);
+void free_dmat(DMat& m);
+int dequant_dmat(const DMat& m, float* d_out, cudaStream_t st);
+int64_t dmat_device_bytes(const DMat& m);
+
+// ---- GEMV / GEMM epilogues (gemm.cu) --------------------------------------------
+enum EpiMode {
+  EPI_F32 = 0,       // out[r*ldo + n] = acc (+ bias[n])                   (cross q, logits)
+  EPI_RESID = 1,     // out[r*ldo + n] += acc + bias[n]                    (residual adds, decoder.go:394-398)
+  EPI_GELU_F16 = 2,  // out16[r*ldo + n] = half(GELU(acc + bias[n]))       (mlp.0, decoder.go:981-985)
+  EPI_QKV = 3,       // n in [0,d): q; [d,2d): K -> cache slot pos; [2d,3d): V + bias -> cache
+  EPI_CROSS_KV = 4   // rows r = u*T + t, cols n = (l*2 + kv)*d + j -> cross K/V cache (+ V bias)
+};
+
+struct Epi {
+  int mode = EPI_F32;
+  int R = 0, N = 0;            // valid activation rows / weight rows
+  const float* bias = nullptr; // [N]
+  float* out = nullptr;        // fp32 output (EPI_F32, EPI_RESID, q of EPI_QKV)
+  __half* out16 = nullptr;     // EPI_GELU_F16
+  int ldo = 0;
+  // EPI_QKV / EPI_CROSS_KV
+  int d = 0, H = 0, hd = 64, T = 0;  // T: positions per (row, head) slab (Tmax or T_enc)
+  const int* pos = nullptr;          // device scalar: slot written by EPI_QKV
+  __half* kv = nullptr;              // QKV: this layer's cache base; CROSS: whole cross cache
+  const float* bias_q = nullptr;     // QKV q bias [d]
+  const float* bias_v = nullptr;     // QKV v bias [d]; CROSS: [L][d]
+  int U = 0;                         // CROSS: utterances
+};
+
+// path: 0 auto, 1 small-R kernel, 2 large-R kernel.
+int init_gemm_attributes();
+int launch_matmul(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st,
+                  int path = 0);
+
+// ---- elementwise (eltwise.cu) -----------------------------------------------------
+// x[r] = dequant(tok_emb row tok[r]) + pos_emb[pos]   (decoder.go:756-773, Q1 fix)
+int launch_embed(const DMat& tok_emb, const float* pos_emb, const int* tokens, const int* pos,
+                 int pos_offset, int R, int d, float* x, cudaStream_t st);
+// out16[r] = half(LayerNorm(x[r]))  (ml/ops.go:153-202); optional fp32 copy
+int launch_layernorm(const float* x, const float* w, const float* b, int R, int d, __half* out16,
+                     float* out32, cudaStream_t st);
+int launch_f32_to_f16(const float* in, __half* out, int64_t n, cudaStream_t st);
+
+// ---- attention (attn.cu) ------------------------------------------------------------
+struct SelfAttnArgs {
+  const float* q;          // [R][d] (unscaled, bias added)
+  const __half* kv;        // this layer's cache base [Rphys][2][H][Tmax][hd]
+  const int* tbl;          // [R][Tmax] physical row of each position (nullptr: own row)
+  const int* pos;          // device scalar: current position
+  int R, H, hd, Tmax;
+  int ref_compat;          // 1: only slot 0 is visible (attention.go:250-256 with Tq=1)
+  int zero_unless_pos0;    // 1: slot 0 is zero unless pos == 0 (beam reset, decoder.go:593)
+  __half* out16;           // [R][d]
+};
+int launch_self_attn(const SelfAttnArgs& a, cudaStream_t st);
+
+struct CrossAttnArgs {
+  const float* q;          // [U*B][d]
+  const __half* kv;        // this layer's cross cache [U][2][H][T][hd]
+  int U, B, H, hd, T;
+  __half* out16;           // [U*B][d]
+};
+int launch_cross_attn(const CrossAttnArgs& a, cudaStream_t st);
+int init_attn_attributes();
+
+// ---- sampling (sample.cu) ----------------------------------------------------------
+struct SampleState {
+  int R, B, U;             // rows, beam width (1 = greedy), utterances
+  int V, eot, Tcap;        // vocab, EOT id, token-history capacity per row
+  int P, max_tokens;       // prompt length, token budget
+  float inv_temp;          // 1/T (decoder.go:1001-1004)
+  int suppress_nst;        // decoder.go:1016-1034
+  float no_speech_thold;
+  int suppress_eot;        // build switch: EOT never selected
+  int correct_mode;        // 1: KV tables are reordered with the beams
+  int Tmax;                // KV positions per row
+  // device state
+  float* logits;           // [R][V] (penalised in place)
+  int* hist;               // [R][Tcap] token history (prompt included)
+  int* hist_tmp;           // [R][Tcap]
+  int* len;                // [R]
+  float* score;            // [R] beam log-prob sums
+  int* tok_in;             // [R] token fed to the next forward
+  int* tbl;                // [R][Tmax] KV position -> physical row (CORRECT beams)
+  int* tbl_tmp;
+  int* utt_done;           // [U]
+  int* utt_steps;          // [U] token steps executed
+  int* n_done;             // device scalar: finished utterances
+  int* pos;                // device scalar
+  int* topk_tok;           // [R][5]
+  float* topk_lp;          // [R][5]
+  int* parent;             // [R]
+  int* new_tok;            // [R]
+  float* new_score;        // [R]
+  int* new_len;            // [R]
+  int* carried;            // [R]
+  const int* forced;       // teacher forcing: [n][R] tokens or nullptr
+  int* step;               // device scalar: steps taken
+};
+// One token step of sampling: penalty, greedy argmax or beam top-5 + merge,
+// history/KV-table reorder, pos += 1.
+int launch_sample_step(const SampleState& s, cudaStream_t st);
+// Teacher forcing: append forced[step][r] to every row r, pos += 1.
+int launch_forced_step(const SampleState& s, cudaStream_t st);
+// pos += 1 (prompt prefill passes).
+int launch_pos_inc(const SampleState& s, cudaStream_t st);
+// Reset of the per-job state before a decode.
+int launch_sample_reset(const SampleState& s, const int* prompt_dev, cudaStream_t st);
+
+}  // namespace wg

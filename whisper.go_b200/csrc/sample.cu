@@ -1,0 +1,384 @@
+// sample.cu — on-device token selection of the decoder token loop.
+//
+//  penalty_kernel      applyRepetitionPenalty (internal/model/decoder.go:1140-1167)
+//  greedy_kernel       sampleGreedyWithScratch (:996-1059) + the greedy loop's
+//                      append / EOT / repeat-streak stops (:467-484)
+//  topk_kernel         topKTokensWithScratch (:1068-1136), k = 5
+//  beam_update_kernel  candidate scoring (:578-623), sortAndPruneBeams
+//                      (:1462-1475), beam rebuild (:629-660), all-EOT and
+//                      best-beam repeat stops (:662-691); the KV position
+//                      table of every beam follows its parent (CORRECT mode)
+#include "kernels.cuh"
+
+namespace wg {
+namespace {
+
+// ---- repetition penalty: logit[id] -= 2.0 * count(id in last 128 tokens) ----
+__global__ void penalty_kernel(SampleState s) {
+  const int r = blockIdx.x, u = r / s.B, lane = threadIdx.x;
+  if (s.utt_done[u]) return;
+  const int* h = s.hist + (int64_t)r * s.Tcap;
+  const int n = s.len[r];
+  const int start = n > 128 ? n - 128 : 0;
+  float* lg = s.logits + (int64_t)r * s.V;
+  for (int i = start + lane; i < n; i += 32) {
+    int id = h[i];
+    if (id < 0 || id >= s.V) continue;
+    bool first = true;
+    for (int j = start; j < i; j++)
+      if (h[j] == id) { first = false; break; }
+    if (!first) continue;
+    int cnt = 0;
+    for (int j = i; j < n; j++) cnt += h[j] == id;
+    lg[id] = __fsub_rn(lg[id], __fmul_rn(2.0f, (float)cnt));
+  }
+  __syncwarp();
+  if (lane == 0 && s.suppress_eot && s.eot >= 0 && s.eot < s.V) lg[s.eot] = -INFINITY;
+}
+
+struct ArgMax {
+  float v;
+  int i;
+};
+__device__ __forceinline__ ArgMax better(ArgMax a, ArgMax b) {
+  // larger value wins; on ties the lower index (the reference keeps the first maximum)
+  if (b.v > a.v || (b.v == a.v && b.i >= 0 && (a.i < 0 || b.i < a.i))) return b;
+  return a;
+}
+__device__ __forceinline__ ArgMax warp_argmax(ArgMax a) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ArgMax b{__shfl_xor_sync(0xffffffffu, a.v, o), __shfl_xor_sync(0xffffffffu, a.i, o)};
+    a = better(a, b);
+  }
+  return a;
+}
+
+// ---- greedy ----------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) greedy_kernel(SampleState s) {
+  const int r = blockIdx.x, u = r;  // B == 1
+  if (s.utt_done[u]) return;
+  const float* lg = s.logits + (int64_t)r * s.V;
+  ArgMax all{-INFINITY, -1}, excl{-INFINITY, -1};
+  for (int i = threadIdx.x; i < s.V; i += blockDim.x) {
+    float v = __fmul_rn(lg[i], s.inv_temp);
+    all = better(all, ArgMax{v, i});
+    if (i != s.eot) excl = better(excl, ArgMax{v, i});
+  }
+  __shared__ ArgMax red[2][32];
+  all = warp_argmax(all);
+  excl = warp_argmax(excl);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { red[0][warp] = all; red[1][warp] = excl; }
+  __syncthreads();
+  if (warp != 0) return;
+  const int nw = blockDim.x >> 5;
+  all = lane < nw ? red[0][lane] : ArgMax{-INFINITY, -1};
+  excl = lane < nw ? red[1][lane] : ArgMax{-INFINITY, -1};
+  all = warp_argmax(all);
+  excl = warp_argmax(excl);
+  if (lane != 0) return;
+  int tok = all.i < 0 ? 0 : all.i;
+  if (s.suppress_nst && s.eot >= 0 && s.eot < s.V) {
+    if (lg[s.eot] < -s.no_speech_thold && tok == s.eot) tok = excl.i < 0 ? s.eot : excl.i;
+  }
+  int* h = s.hist + (int64_t)r * s.Tcap;
+  int n = s.len[r];
+  h[n] = tok;
+  n++;
+  s.len[r] = n;
+  s.tok_in[r] = tok;
+  s.utt_steps[u] += 1;
+  bool done = tok == s.eot || n >= s.P + s.max_tokens;
+  if (!done) {
+    int streak = 0;  // trailing identical generated tokens (prevToken starts at -1)
+    for (int i = n - 1; i >= s.P && h[i] == tok; i--) streak++;
+    done = streak > 20;
+  }
+  if (done) {
+    s.utt_done[u] = 1;
+    atomicAdd(s.n_done, 1);
+  }
+}
+
+// ---- beam: per-row top-5 of log_softmax(logits / T) ----------------------------
+constexpr int TOPK = 5;
+
+__device__ __forceinline__ void top_insert(float* v, int* ix, float nv, int ni) {
+  // keep v[0..4] sorted: larger first, lower index first on ties
+  if (!(nv > v[TOPK - 1] || (nv == v[TOPK - 1] && ni < ix[TOPK - 1] && ix[TOPK - 1] >= 0))) return;
+  int j = TOPK - 1;
+  while (j > 0 && (nv > v[j - 1] || (nv == v[j - 1] && ni < ix[j - 1]))) {
+    v[j] = v[j - 1];
+    ix[j] = ix[j - 1];
+    j--;
+  }
+  v[j] = nv;
+  ix[j] = ni;
+}
+
+__global__ void __launch_bounds__(1024) topk_kernel(SampleState s) {
+  const int r = blockIdx.x, u = r / s.B;
+  if (s.utt_done[u]) return;
+  const int n = s.len[r];
+  const int* h = s.hist + (int64_t)r * s.Tcap;
+  if (n > 0 && h[n - 1] == s.eot) return;  // finished hypothesis: carried forward unchanged
+  const float* lg = s.logits + (int64_t)r * s.V;
+  float tv[TOPK];
+  int ti[TOPK];
+#pragma unroll
+  for (int j = 0; j < TOPK; j++) { tv[j] = -INFINITY; ti[j] = -1; }
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < s.V; i += blockDim.x) {
+    float v = __fmul_rn(lg[i], s.inv_temp);
+    mx = fmaxf(mx, v);
+    top_insert(tv, ti, v, i);
+  }
+  __shared__ float cv[32 * TOPK];
+  __shared__ int ci[32 * TOPK];
+  __shared__ float wsum[32];
+  __shared__ float smax;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  // warp merge: 5 rounds of arg-max over the lanes' list heads
+  int head = 0;
+  for (int k = 0; k < TOPK; k++) {
+    ArgMax a{head < TOPK ? tv[head] : -INFINITY, head < TOPK ? ti[head] : -1};
+    ArgMax b = warp_argmax(a);
+    if (a.i == b.i && b.i >= 0) head++;
+    if (lane == 0) { cv[warp * TOPK + k] = b.v; ci[warp * TOPK + k] = b.i; }
+  }
+  float m = warp_max(mx);
+  if (lane == 0) wsum[warp] = m;
+  __syncthreads();
+  if (warp == 0) {
+    float mm = lane < nw ? wsum[lane] : -INFINITY;
+    mm = warp_max(mm);
+    if (lane == 0) smax = mm;
+  }
+  __syncthreads();
+  mx = smax;
+  // expSum = sum float32(exp(float64(s - max)))  (decoder.go:1121-1124)
+  float es = 0.f;
+  for (int i = threadIdx.x; i < s.V; i += blockDim.x)
+    es += (float)exp((double)__fsub_rn(__fmul_rn(lg[i], s.inv_temp), mx));
+  es = warp_sum(es);
+  __syncthreads();
+  if (lane == 0) wsum[warp] = es;
+  __syncthreads();
+  if (warp != 0) return;
+  float tot = 0.f;
+  if (lane == 0)
+    for (int w = 0; w < nw; w++) tot += wsum[w];
+  tot = __shfl_sync(0xffffffffu, tot, 0);
+  const float logZ = __fadd_rn((float)log((double)tot), mx);
+  // merge the warps' lists (nw * 5 candidates, 5 per lane)
+  float lv[TOPK];
+  int li[TOPK];
+#pragma unroll
+  for (int j = 0; j < TOPK; j++) {
+    bool ok = lane < nw;
+    lv[j] = ok ? cv[lane * TOPK + j] : -INFINITY;
+    li[j] = ok ? ci[lane * TOPK + j] : -1;
+  }
+  head = 0;
+  for (int k = 0; k < TOPK; k++) {
+    ArgMax a{head < TOPK ? lv[head] : -INFINITY, head < TOPK ? li[head] : -1};
+    ArgMax b = warp_argmax(a);
+    if (a.i == b.i && b.i >= 0) head++;
+    if (lane == 0) {
+      s.topk_tok[r * TOPK + k] = b.i;
+      s.topk_lp[r * TOPK + k] = __fsub_rn(b.v, logZ);
+    }
+  }
+}
+
+// ---- beam: candidates, prune, rebuild, stops (one CTA per utterance) -------------
+constexpr int MAXB = 16;
+
+__global__ void __launch_bounds__(128) beam_update_kernel(SampleState s) {
+  const int u = blockIdx.x;
+  if (s.utt_done[u]) return;
+  const int B = s.B;
+  __shared__ float c_norm[MAXB * TOPK], c_score[MAXB * TOPK], c_lp[MAXB * TOPK];
+  __shared__ int c_parent[MAXB * TOPK], c_tok[MAXB * TOPK], c_carried[MAXB * TOPK];
+  __shared__ int nc_sh;
+  __shared__ int sel[MAXB];
+  __shared__ int stop_sh;
+  if (threadIdx.x == 0) {
+    int nc = 0;
+    for (int b = 0; b < B; b++) {
+      int r = u * B + b;
+      int n = s.len[r];
+      const int* h = s.hist + (int64_t)r * s.Tcap;
+      float sc = s.score[r];
+      if (n > 0 && h[n - 1] == s.eot) {
+        c_parent[nc] = b; c_score[nc] = sc; c_tok[nc] = s.eot; c_lp[nc] = 0.f; c_carried[nc] = 1;
+        c_norm[nc] = __fdiv_rn(sc, (float)pow((double)n, 0.6));
+        nc++;
+        continue;
+      }
+      float den = (float)pow((double)(n + 1), 0.6);
+      for (int j = 0; j < TOPK; j++) {
+        int tk = s.topk_tok[r * TOPK + j];
+        if (tk < 0) continue;
+        float lp = s.topk_lp[r * TOPK + j];
+        float ns = __fadd_rn(sc, lp);
+        c_parent[nc] = b; c_score[nc] = ns; c_tok[nc] = tk; c_lp[nc] = lp; c_carried[nc] = 0;
+        c_norm[nc] = __fdiv_rn(ns, den);
+        nc++;
+      }
+    }
+    nc_sh = nc;
+  }
+  __syncthreads();
+  const int nc = nc_sh;
+  // stable rank by normScore (descending)
+  for (int i = threadIdx.x; i < nc; i += blockDim.x) {
+    int rank = 0;
+    for (int j = 0; j < nc; j++) rank += (c_norm[j] > c_norm[i]) || (c_norm[j] == c_norm[i] && j < i);
+    if (rank < B) sel[rank] = i;
+  }
+  __syncthreads();
+  const int nb = nc < B ? nc : B;
+  // rebuild: token histories (and KV tables) from the parents, via shared memory
+  extern __shared__ int dyn[];
+  int* th = dyn;                      // [B][Tcap]
+  int* tt = dyn + B * s.Tcap;         // [B][Tmax]
+  __shared__ int nlen[MAXB];
+  const int pos = *s.pos;
+  for (int b = 0; b < nb; b++) {
+    int ci_ = sel[b];
+    int pr = u * B + c_parent[ci_];
+    int pl = s.len[pr];
+    const int* ph = s.hist + (int64_t)pr * s.Tcap;
+    for (int i = threadIdx.x; i < pl; i += blockDim.x) th[b * s.Tcap + i] = ph[i];
+    if (s.correct_mode) {
+      const int* pt = s.tbl + (int64_t)pr * s.Tmax;
+      for (int i = threadIdx.x; i <= pos && i < s.Tmax; i += blockDim.x) tt[b * s.Tmax + i] = pt[i];
+    }
+    if (threadIdx.x == 0) {
+      bool carried = pl > 0 && ph[pl - 1] == s.eot && c_tok[ci_] == s.eot && c_lp[ci_] == 0.f;
+      if (carried) nlen[b] = pl;
+      else { th[b * s.Tcap + pl] = c_tok[ci_]; nlen[b] = pl + 1; }
+    }
+  }
+  __syncthreads();
+  for (int b = 0; b < nb; b++) {
+    int r = u * B + b;
+    int* dh = s.hist + (int64_t)r * s.Tcap;
+    for (int i = threadIdx.x; i < nlen[b]; i += blockDim.x) dh[i] = th[b * s.Tcap + i];
+    if (s.correct_mode) {
+      int* dt = s.tbl + (int64_t)r * s.Tmax;
+      for (int i = threadIdx.x; i <= pos && i < s.Tmax; i += blockDim.x) dt[i] = tt[b * s.Tmax + i];
+      if (threadIdx.x == 0 && pos + 1 < s.Tmax) dt[pos + 1] = r;  // the next step writes here
+    }
+    if (threadIdx.x == 0) {
+      s.len[r] = nlen[b];
+      s.score[r] = c_score[sel[b]];
+      s.tok_in[r] = th[b * s.Tcap + nlen[b] - 1];
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    s.utt_steps[u] += 1;
+    bool all_eot = true;  // decoder.go:662-672
+    for (int b = 0; b < nb; b++) {
+      int r = u * B + b;
+      if (s.len[r] == 0 || s.hist[(int64_t)r * s.Tcap + s.len[r] - 1] != s.eot) { all_eot = false; break; }
+    }
+    bool stop = all_eot;
+    if (!stop && nb > 0) {  // best beam repeats > 20 (decoder.go:675-691)
+      int r = u * B;
+      const int* h = s.hist + (int64_t)r * s.Tcap;
+      int n = s.len[r];
+      if (n >= 2) {
+        int last = h[n - 1], streak = 1;
+        for (int i = n - 2; i >= 0 && h[i] == last; i--) {
+          streak++;
+          if (streak > 20) { stop = true; break; }
+        }
+      }
+    }
+    if (s.utt_steps[u] >= s.max_tokens) stop = true;
+    stop_sh = stop;
+    if (stop) {
+      s.utt_done[u] = 1;
+      atomicAdd(s.n_done, 1);
+    }
+  }
+}
+
+__global__ void pos_inc_kernel(int* pos, int* step) {
+  *pos += 1;
+  *step += 1;
+}
+
+__global__ void forced_kernel(SampleState s) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= s.R) return;
+  const int tok = s.forced[(int64_t)(*s.step) * s.R + r];
+  int n = s.len[r];
+  if (n < s.Tcap) s.hist[(int64_t)r * s.Tcap + n] = tok;
+  s.len[r] = n + 1;
+  s.tok_in[r] = tok;
+}
+
+__global__ void reset_kernel(SampleState s, const int* __restrict__ prompt) {
+  const int r = blockIdx.x;
+  int* h = s.hist + (int64_t)r * s.Tcap;
+  for (int i = threadIdx.x; i < s.P; i += blockDim.x) h[i] = prompt[i];
+  int* t = s.tbl + (int64_t)r * s.Tmax;
+  for (int i = threadIdx.x; i < s.Tmax; i += blockDim.x) t[i] = r;
+  if (threadIdx.x == 0) {
+    s.len[r] = s.P;
+    s.score[r] = 0.f;
+    s.tok_in[r] = prompt[s.P - 1];
+    if (r % s.B == 0) {
+      s.utt_done[r / s.B] = 0;
+      s.utt_steps[r / s.B] = 0;
+    }
+    if (r == 0) {
+      *s.n_done = 0;
+      *s.pos = s.correct_mode ? 0 : s.P - 1;
+      *s.step = 0;
+    }
+  }
+}
+
+}  // namespace
+
+int launch_sample_step(const SampleState& s, cudaStream_t st) {
+  penalty_kernel<<<s.R, 32, 0, st>>>(s);
+  WG_CHECK(launch_status("penalty"));
+  if (s.B <= 1) {
+    greedy_kernel<<<s.R, 1024, 0, st>>>(s);
+    WG_CHECK(launch_status("greedy"));
+  } else {
+    topk_kernel<<<s.R, 1024, 0, st>>>(s);
+    WG_CHECK(launch_status("topk"));
+    size_t dyn = (size_t)s.B * (s.Tcap + s.Tmax) * sizeof(int);
+    beam_update_kernel<<<s.U, 128, dyn, st>>>(s);
+    WG_CHECK(launch_status("beam_update"));
+  }
+  pos_inc_kernel<<<1, 1, 0, st>>>(s.pos, s.step);
+  return launch_status("pos_inc");
+}
+
+int launch_forced_step(const SampleState& s, cudaStream_t st) {
+  forced_kernel<<<(s.R + 127) / 128, 128, 0, st>>>(s);
+  WG_CHECK(launch_status("forced"));
+  pos_inc_kernel<<<1, 1, 0, st>>>(s.pos, s.step);
+  return launch_status("pos_inc");
+}
+
+int launch_pos_inc(const SampleState& s, cudaStream_t st) {
+  pos_inc_kernel<<<1, 1, 0, st>>>(s.pos, s.step);
+  return launch_status("pos_inc");
+}
+
+int launch_sample_reset(const SampleState& s, const int* prompt_dev, cudaStream_t st) {
+  reset_kernel<<<s.R, 128, 0, st>>>(s, prompt_dev);
+  return launch_status("sample_reset");
+}
+
+}  // namespace wg
