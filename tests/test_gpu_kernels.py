@@ -71,6 +71,22 @@ def test_matmul_vs_oracle(qt, R, path):
 
 
 @pytest.mark.parametrize("qt", QT)
+@pytest.mark.parametrize("R", [17, 40, 130, 320])
+def test_matmul_tcgen05_vs_oracle(qt, R):
+    """The tcgen05 path (TMA-fed, TMEM accumulators) on partial weight and row tiles."""
+    raw, a, ref = _matmul_case(qt, R, 200, 256, seed=R * 13)
+    gpu = wgdec.matmul(qt, raw, 200, 256, a, path=3)
+    assert _close(gpu, ref), float(np.max(np.abs(gpu - ref)))
+
+
+@pytest.mark.parametrize("R,rows,K", [(320, 1280, 1280), (600, 384, 5120), (40, 5120, 1280), (1500, 256, 384)])
+def test_matmul_tcgen05_model_shapes(R, rows, K):
+    raw, a, ref = _matmul_case("Q8_0", R, rows, K, seed=R + K)
+    gpu = wgdec.matmul("Q8_0", raw, rows, K, a, path=3)
+    assert _close(gpu, ref), float(np.max(np.abs(gpu - ref)))
+
+
+@pytest.mark.parametrize("qt", QT)
 def test_matmul_reference_tolerances(kat, qt):
     # internal/ml/matmul_q8_test.go:151-207 on the device (K=64 -> two quant blocks)
     c = kat["matmul_all"]

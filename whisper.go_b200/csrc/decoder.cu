@@ -164,6 +164,7 @@ int build_devmodel(const wg_model_desc* md, int dev, DevModel** out) {
   if (cudaStreamCreateWithFlags(&dm->st, cudaStreamNonBlocking) != cudaSuccess) return fail(WG_ERR_CUDA);
   if ((rc = init_gemm_attributes()) != WG_OK) return fail(rc);
   if ((rc = init_attn_attributes()) != WG_OK) return fail(rc);
+  if ((rc = init_tc_attributes()) != WG_OK) return fail(rc);
   const int d = md->n_state, L = md->n_layer, ctx = md->n_text_ctx;
   // fp32 vectors: 6 LN + 7 biases (d or 4d) per layer, final LN, pos emb, cross V bias
   std::vector<float> host;
@@ -684,6 +685,15 @@ static int poll_done(wg_job* J) {
     total += *j->host_done;
   }
   if (total >= J->U) J->all_done = true;
+  for (DevJob* j : J->dj) {
+    cudaSetDevice(j->dev);
+    int w = 0;
+    WG_CHECK(tc_error_word(&w, true));
+    if (w) {
+      set_error("a tcgen05 kernel's bounded wait expired (code 0x%x)", w);
+      return WG_ERR_DEVICE_FLAG;
+    }
+  }
   return WG_OK;
 }
 
@@ -902,6 +912,7 @@ int wg_matmul_test(uint32_t qtype, const void* raw, int rows, int cols, const fl
   }
   WG_CHECK_CUDA(cudaSetDevice(0));
   WG_CHECK(init_gemm_attributes());
+  WG_CHECK(init_tc_attributes());
   cudaStream_t st = nullptr;
   WG_CHECK_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
   wg_matrix wm{qtype, rows, cols, raw};
@@ -929,6 +940,14 @@ int wg_matmul_test(uint32_t qtype, const void* raw, int rows, int cols, const fl
     rc = WG_ERR_CUDA;
   }
   if (rc == WG_OK) rc = wait_stream(st);
+  if (rc == WG_OK) {
+    int w = 0;
+    rc = tc_error_word(&w, true);
+    if (rc == WG_OK && w) {
+      set_error("a tcgen05 kernel's bounded wait expired (code 0x%x)", w);
+      rc = WG_ERR_DEVICE_FLAG;
+    }
+  }
   cudaFree(dx); cudaFree(dx16); cudaFree(dout);
   free_dmat(dm);
   cudaStreamDestroy(st);

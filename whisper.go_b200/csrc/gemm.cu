@@ -352,7 +352,14 @@ int launch_small_t(const DMat& W, const __half* X, int ldx, int R, const Epi& e,
 
 template <uint32_t QT>
 int launch_q(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st, int path) {
-  if (path == 0) path = R <= 16 ? 1 : 2;
+  if (path == 0) path = R <= 16 ? 1 : (tc_supported(W) ? 3 : 2);
+  if (path == 3) {
+    if (!tc_supported(W)) {
+      set_error("tcgen05 path needs a quantised matrix with K %% 64 == 0 (K=%d)", W.cols);
+      return WG_ERR_UNSUPPORTED;
+    }
+    return launch_matmul_tc(W, X, ldx, R, e, st);
+  }
   if (path == 1) {
     if (R <= 8) return launch_small_t<QT, 1>(W, X, ldx, R, e, st);
     if (R <= 16) return launch_small_t<QT, 2>(W, X, ldx, R, e, st);

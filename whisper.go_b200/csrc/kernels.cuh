@@ -37,8 +37,14 @@ struct Epi {
   int U = 0;                         // CROSS: utterances
 };
 
-// path: 0 auto, 1 small-R kernel, 2 large-R kernel.
+// path: 0 auto, 1 small-R kernel (mma.sync GEMV), 2 large-R mma.sync kernel,
+// 3 tcgen05 tensor-core kernel (quantised weights, K % 64 == 0).
 int init_gemm_attributes();
+int init_tc_attributes();
+bool tc_supported(const DMat& W);
+int launch_matmul_tc(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st);
+// First expired bounded wait of a tcgen05 kernel on the current device (0: none).
+int tc_error_word(int* word, bool clear);
 int launch_matmul(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st,
                   int path = 0);
 

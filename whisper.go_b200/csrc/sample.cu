@@ -181,14 +181,45 @@ __global__ void __launch_bounds__(1024) topk_kernel(SampleState s) {
     li[j] = ok ? ci[lane * TOPK + j] : -1;
   }
   head = 0;
+  float fv[TOPK];
+  int fi[TOPK];
   for (int k = 0; k < TOPK; k++) {
     ArgMax a{head < TOPK ? lv[head] : -INFINITY, head < TOPK ? li[head] : -1};
     ArgMax b = warp_argmax(a);
     if (a.i == b.i && b.i >= 0) head++;
-    if (lane == 0) {
-      s.topk_tok[r * TOPK + k] = b.i;
-      s.topk_lp[r * TOPK + k] = __fsub_rn(b.v, logZ);
+    fv[k] = b.v;
+    fi[k] = b.i;
+  }
+  if (lane != 0) return;
+  bool tie = false;
+  for (int k = 0; k + 1 < TOPK; k++) tie |= fi[k + 1] >= 0 && fv[k] == fv[k + 1];
+  if (tie) {
+    // Equal values keep the slot order of the reference's replace-min scan
+    // (decoder.go:1087-1119) through its sort (stable for 5 elements):
+    // rerun that scan exactly. Only reached when top-5 values tie exactly.
+    int n = 0, minPos = -1;
+    float minVal = 0.f;
+    for (int i = 0; i < s.V; i++) {
+      float v = __fmul_rn(lg[i], s.inv_temp);
+      if (n < TOPK) {
+        fv[n] = v; fi[n] = i; n++;
+        if (minPos < 0 || v < minVal) { minPos = n - 1; minVal = v; }
+        continue;
+      }
+      if (v <= minVal) continue;
+      fv[minPos] = v; fi[minPos] = i;
+      minPos = 0; minVal = fv[0];
+      for (int j = 1; j < n; j++) if (fv[j] < minVal) { minVal = fv[j]; minPos = j; }
     }
+    for (int a = 1; a < n; a++) {  // stable insertion sort, descending
+      float vv = fv[a]; int ii = fi[a]; int b = a - 1;
+      while (b >= 0 && fv[b] < vv) { fv[b + 1] = fv[b]; fi[b + 1] = fi[b]; b--; }
+      fv[b + 1] = vv; fi[b + 1] = ii;
+    }
+  }
+  for (int k = 0; k < TOPK; k++) {
+    s.topk_tok[r * TOPK + k] = fi[k];
+    s.topk_lp[r * TOPK + k] = __fsub_rn(fv[k], logZ);
   }
 }
 
@@ -310,7 +341,7 @@ __global__ void __launch_bounds__(128) beam_update_kernel(SampleState s) {
 
 __global__ void pos_inc_kernel(int* pos, int* step) {
   *pos += 1;
-  *step += 1;
+  if (step) *step += 1;
 }
 
 __global__ void forced_kernel(SampleState s) {
@@ -372,7 +403,7 @@ int launch_forced_step(const SampleState& s, cudaStream_t st) {
 }
 
 int launch_pos_inc(const SampleState& s, cudaStream_t st) {
-  pos_inc_kernel<<<1, 1, 0, st>>>(s.pos, s.step);
+  pos_inc_kernel<<<1, 1, 0, st>>>(s.pos, nullptr);
   return launch_status("pos_inc");
 }
 
