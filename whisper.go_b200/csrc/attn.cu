@@ -45,7 +45,8 @@ struct SimtArgs {
   int ldo;
 };
 
-constexpr int SIMT_WARPS = 4;
+constexpr int SIMT_WARPS = 8;
+constexpr int SIMT_UNROLL = 4;  // warp steps whose loads are issued together
 
 __global__ void __launch_bounds__(SIMT_WARPS * 32) attn_simt_kernel(SimtArgs a) {
   extern __shared__ float sm[];  // scores [n] then reduction scratch
@@ -72,32 +73,48 @@ __global__ void __launch_bounds__(SIMT_WARPS * 32) attn_simt_kernel(SimtArgs a) 
   auto slab_of = [&](int t) -> int64_t {
     return a.tbl ? (int64_t)a.tbl[(int64_t)r * a.tbl_ld + t] : (int64_t)(r / a.rows_per_slab);
   };
-  // scores
-  for (int t0 = warp * 4; t0 < n; t0 += SIMT_WARPS * 4) {
-    int t = t0 + sub;
-    float part = 0.f;
-    if (t < n) {
-      const __half* kr = a.kv + slab_of(t) * a.slab_stride + (int64_t)h * a.head_stride + (int64_t)t * hd;
-      if (hd == 64) {
-        uint4 raw = *reinterpret_cast<const uint4*>(kr + dl);
-        const __half2* k2 = reinterpret_cast<const __half2*>(&raw);
+  // scores: each warp step covers 4 positions (8 lanes x 8 dims each); the
+  // table lookups and K rows of SIMT_UNROLL steps are loaded before use
+  const int step = SIMT_WARPS * 4;
+  for (int tb = warp * 4; tb < n; tb += step * SIMT_UNROLL) {
+    int64_t off[SIMT_UNROLL];
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-          float2 kf = __half22float2(k2[e]);
-          part = fmaf(qs[dl + 2 * e], kf.x, part);
-          part = fmaf(qs[dl + 2 * e + 1], kf.y, part);
-        }
-      } else {
-        for (int e = 0; e < 8; e++) {
-          int c = dl + e;
-          if (c < hd) part = fmaf(qs[c], __half2float(kr[c]), part);
+    for (int u = 0; u < SIMT_UNROLL; u++) {
+      const int t = tb + u * step + sub;
+      off[u] = t < n ? slab_of(t) * a.slab_stride + (int64_t)h * a.head_stride + (int64_t)t * hd : -1;
+    }
+    uint4 kraw[SIMT_UNROLL];
+    if (hd == 64) {
+#pragma unroll
+      for (int u = 0; u < SIMT_UNROLL; u++)
+        kraw[u] = off[u] >= 0 ? *reinterpret_cast<const uint4*>(a.kv + off[u] + dl) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < SIMT_UNROLL; u++) {
+      const int t = tb + u * step + sub;
+      float part = 0.f;
+      if (off[u] >= 0) {
+        if (hd == 64) {
+          const __half2* k2 = reinterpret_cast<const __half2*>(&kraw[u]);
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            float2 kf = __half22float2(k2[e]);
+            part = fmaf(qs[dl + 2 * e], kf.x, part);
+            part = fmaf(qs[dl + 2 * e + 1], kf.y, part);
+          }
+        } else {
+          const __half* kr = a.kv + off[u];
+          for (int e = 0; e < 8; e++) {
+            int c = dl + e;
+            if (c < hd) part = fmaf(qs[c], __half2float(kr[c]), part);
+          }
         }
       }
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      part += __shfl_xor_sync(0xffffffffu, part, 4);
+      if (t < n && (lane & 7) == 0) scores[t] = __fmul_rn(part, scale);
     }
-    part += __shfl_xor_sync(0xffffffffu, part, 1);
-    part += __shfl_xor_sync(0xffffffffu, part, 2);
-    part += __shfl_xor_sync(0xffffffffu, part, 4);
-    if (t < n && (lane & 7) == 0) scores[t] = __fmul_rn(part, scale);
   }
   __syncthreads();
   // max
@@ -129,23 +146,36 @@ __global__ void __launch_bounds__(SIMT_WARPS * 32) attn_simt_kernel(SimtArgs a) 
   float o[8];
 #pragma unroll
   for (int e = 0; e < 8; e++) o[e] = 0.f;
-  for (int t0 = warp * 4; t0 < n; t0 += SIMT_WARPS * 4) {
-    int t = t0 + sub;
-    if (t >= n) continue;
-    const float w = scores[t];
-    const __half* vr = a.kv + slab_of(t) * a.slab_stride + a.v_off + (int64_t)h * a.head_stride + (int64_t)t * hd;
-    if (hd == 64) {
-      uint4 raw = *reinterpret_cast<const uint4*>(vr + dl);
-      const __half2* v2 = reinterpret_cast<const __half2*>(&raw);
+  for (int tb = warp * 4; tb < n; tb += step * SIMT_UNROLL) {
+    int64_t off[SIMT_UNROLL];
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        float2 vf = __half22float2(v2[e]);
-        o[2 * e] = fmaf(w, vf.x, o[2 * e]);
-        o[2 * e + 1] = fmaf(w, vf.y, o[2 * e + 1]);
+    for (int u = 0; u < SIMT_UNROLL; u++) {
+      const int t = tb + u * step + sub;
+      off[u] = t < n ? slab_of(t) * a.slab_stride + a.v_off + (int64_t)h * a.head_stride + (int64_t)t * hd : -1;
+    }
+    uint4 vraw[SIMT_UNROLL];
+    if (hd == 64) {
+#pragma unroll
+      for (int u = 0; u < SIMT_UNROLL; u++)
+        vraw[u] = off[u] >= 0 ? *reinterpret_cast<const uint4*>(a.kv + off[u] + dl) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < SIMT_UNROLL; u++) {
+      if (off[u] < 0) continue;
+      const float w = scores[tb + u * step + sub];
+      if (hd == 64) {
+        const __half2* v2 = reinterpret_cast<const __half2*>(&vraw[u]);
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          float2 vf = __half22float2(v2[e]);
+          o[2 * e] = fmaf(w, vf.x, o[2 * e]);
+          o[2 * e + 1] = fmaf(w, vf.y, o[2 * e + 1]);
+        }
+      } else {
+        const __half* vr = a.kv + off[u];
+        for (int e = 0; e < 8; e++)
+          if (dl + e < hd) o[e] = fmaf(w, __half2float(vr[dl + e]), o[e]);
       }
-    } else {
-      for (int e = 0; e < 8; e++)
-        if (dl + e < hd) o[e] = fmaf(w, __half2float(vr[dl + e]), o[e]);
     }
   }
 #pragma unroll

@@ -49,28 +49,36 @@ inline int launch_status(const char* what) {
 
 // ---- device weight layout ----------------------------------------------------
 //
-// Quantised matrices [rows, cols] (cols % 32 == 0) are repacked at upload into
-// the "tile16" layout consumed by the tensor-core GEMV/GEMM: rows are grouped
-// in tiles of 16, columns in quant blocks of 32, and for every (tile, block)
-// each of the 32 lanes of a warp owns a contiguous payload that is exactly its
+// Quantised matrices [rows, cols] (cols % 64 == 0) are repacked at upload into
+// the "tile128" layout consumed by the tensor-core GEMV/GEMM: rows are grouped
+// in tiles of 16, columns in quant blocks of 32; for every (tile, block) each
+// of the 32 lanes of a warp owns a contiguous payload that is exactly its
 // A-fragment of two mma.m16n8k16 steps (rows g and g+8, k = 2t,2t+1,2t+8,2t+9
-// and +16; g = lane/4, t = lane%4):
-//   qs : [NT][KB][32][PB] bytes, PB = 16 (Q8_0: int8 codes) or 8 (4/5-bit:
+// and +16; g = lane/4, t = lane%4). The (tile, block) "slots" are ordered so
+// that the 8 tiles x 2 blocks of one 128-row x 64-column group are one
+// contiguous run (one bulk copy per tensor-core pipeline stage):
+//   slot(tile, kb) = (((tile/8) * (kb_count/2) + kb/2) * 8 + tile%8) * 2 + kb%2
+//   qs : [slot][32][PB] bytes, PB = 16 (Q8_0: int8 codes) or 8 (4/5-bit:
 //        nibble pairs, pair p of step s at bits 4p and 16+4p of word s)
-//   dsc: [NT][KB][8] half2 = (d[row g], d[row g+8])     (all quant types)
-//   msc: [NT][KB][8] half2 = (m[row g], m[row g+8])     (Q4_1, Q5_1)
-//   hb : [NT][KB][32] u16 lane payload of 5th bits      (Q5_0, Q5_1)
-// Byte count equals the GGUF block bytes (plus the row padding to 16).
+//   dsc: [slot][8] half2 = (d[row g], d[row g+8])     (all quant types)
+//   msc: [slot][8] half2 = (m[row g], m[row g+8])     (Q4_1, Q5_1)
+//   hb : [slot][32] u16 lane payload of 5th bits      (Q5_0, Q5_1)
+// Byte count equals the GGUF block bytes (plus the row padding to 128).
 // F32 / F16 matrices stay dense row-major in qs.
 struct DMat {
   uint32_t qtype = 0;
   int rows = 0, cols = 0;
-  int ntiles = 0, kblocks = 0;
+  int ntiles = 0, kblocks = 0;  // 16-row tiles holding data; allocation covers round_up(ntiles, 8)
   uint8_t* qs = nullptr;
   __half2* dsc = nullptr;
   __half2* msc = nullptr;
   uint16_t* hb = nullptr;
 };
+
+__host__ __device__ inline int64_t slot_of(const DMat& m, int tile, int kb) {
+  return ((((int64_t)(tile >> 3) * (m.kblocks >> 1) + (kb >> 1)) * 8 + (tile & 7)) << 1) + (kb & 1);
+}
+__host__ __device__ inline int64_t dmat_slots(const DMat& m) { return (int64_t)((m.ntiles + 7) / 8) * 8 * m.kblocks; }
 
 __host__ __device__ inline bool qtype_is_quant(uint32_t q) {
   return q == WG_QTYPE_Q4_0 || q == WG_QTYPE_Q4_1 || q == WG_QTYPE_Q5_0 || q == WG_QTYPE_Q5_1 ||

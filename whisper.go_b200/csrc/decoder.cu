@@ -878,8 +878,22 @@ int wg_dequant_test(uint32_t qtype, const void* raw, int64_t n, float* out) {
   wg_matrix wm{};
   wm.qtype = qtype;
   wm.data = raw;
-  if (qtype_is_quant(qtype)) { wm.cols = 32; wm.rows = (int)((n + 31) / 32); }
-  else { wm.cols = (int)n; wm.rows = 1; }
+  std::vector<uint8_t> padded;
+  if (qtype_is_quant(qtype)) {
+    // rows of two quant blocks (the device layout needs cols % 64 == 0); an
+    // odd trailing block is padded with a zero block
+    const int64_t nb = (n + 31) / 32, bb = gguf_block_bytes(qtype);
+    wm.cols = 64;
+    wm.rows = (int)((nb + 1) / 2);
+    if (nb % 2) {
+      padded.assign((size_t)(nb + 1) * bb, 0);
+      memcpy(padded.data(), raw, (size_t)nb * bb);
+      wm.data = padded.data();
+    }
+  } else {
+    wm.cols = (int)n;
+    wm.rows = 1;
+  }
   const wg_matrix* parts[1] = {&wm};
   DMat dm;
   cudaStream_t st = nullptr;

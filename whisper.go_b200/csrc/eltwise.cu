@@ -5,7 +5,7 @@ namespace wg {
 namespace {
 
 // Exact fp32 dequantisation of element (r, k) of a device matrix
-// (internal/gguf/dequant.go:92-201 through the tile16 layout).
+// (internal/gguf/dequant.go:92-201 through the tile128 layout).
 __device__ __forceinline__ float dmat_elem(const DMat& m, int r, int k) {
   if (m.qtype == WG_QTYPE_F32) return reinterpret_cast<const float*>(m.qs)[(int64_t)r * m.cols + k];
   if (m.qtype == WG_QTYPE_F16) return __half2float(reinterpret_cast<const __half*>(m.qs)[(int64_t)r * m.cols + k]);
@@ -13,7 +13,7 @@ __device__ __forceinline__ float dmat_elem(const DMat& m, int r, int k) {
   int kb = k >> 5, kk = k & 31, s = kk >> 4, kr = kk & 15;
   int t = (kr & 7) >> 1, e = kr & 1, reg = ((kr >> 3) << 1) | hi;
   int lane = g * 4 + t;
-  int64_t slot = (int64_t)tile * m.kblocks + kb;
+  int64_t slot = slot_of(m, tile, kb);
   __half2 dd = m.dsc[slot * 8 + g];
   float d = __half2float(hi ? __high2half(dd) : __low2half(dd));
   if (m.qtype == WG_QTYPE_Q8_0) {
@@ -73,6 +73,59 @@ __global__ void layernorm_kernel(const float* __restrict__ x, const float* __res
   }
 }
 
+// Same arithmetic with the row held in registers (d == 128 * NV): one read
+// of x instead of three dependent passes.
+template <int NV>
+__global__ void layernorm_reg_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                     const float* __restrict__ b, int R, __half* __restrict__ out16, int ld16,
+                                     float* __restrict__ out32) {
+  constexpr int d = NV * 128;
+  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= R) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + (int64_t)r * d);
+  float4 v[NV];
+#pragma unroll
+  for (int i = 0; i < NV; i++) v[i] = xr[lane + 32 * i];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; i++) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  s = warp_sum(s);
+  const float mean = __fdiv_rn(s, (float)d);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    float a = __fsub_rn(v[i].x, mean), bb = __fsub_rn(v[i].y, mean), c = __fsub_rn(v[i].z, mean),
+          e = __fsub_rn(v[i].w, mean);
+    q = __fmaf_rn(a, a, q);
+    q = __fmaf_rn(bb, bb, q);
+    q = __fmaf_rn(c, c, q);
+    q = __fmaf_rn(e, e, q);
+  }
+  q = warp_sum(q);
+  const float sd = __fsqrt_rn(__fadd_rn(__fdiv_rn(q, (float)d), 1e-5f));
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    const int c4 = lane + 32 * i;
+    const float4 ww = w4[c4], bv = b4[c4];
+    float4 o;
+    o.x = __fadd_rn(__fdiv_rn(__fmul_rn(ww.x, __fsub_rn(v[i].x, mean)), sd), bv.x);
+    o.y = __fadd_rn(__fdiv_rn(__fmul_rn(ww.y, __fsub_rn(v[i].y, mean)), sd), bv.y);
+    o.z = __fadd_rn(__fdiv_rn(__fmul_rn(ww.z, __fsub_rn(v[i].z, mean)), sd), bv.z);
+    o.w = __fadd_rn(__fdiv_rn(__fmul_rn(ww.w, __fsub_rn(v[i].w, mean)), sd), bv.w);
+    if (out16) {
+      __half2 h0 = __floats2half2_rn(o.x, o.y), h1 = __floats2half2_rn(o.z, o.w);
+      uint2 u;
+      memcpy(&u.x, &h0, 4);
+      memcpy(&u.y, &h1, 4);
+      *reinterpret_cast<uint2*>(out16 + (int64_t)r * ld16 + 4 * c4) = u;
+    }
+    if (out32) reinterpret_cast<float4*>(out32 + (int64_t)r * d)[c4] = o;
+  }
+}
+
 __global__ void f32_to_f16_kernel(const float* __restrict__ in, __half* __restrict__ out, int64_t n) {
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -90,7 +143,15 @@ int launch_embed(const DMat& te, const float* pos_emb, const int* tokens, const 
 int launch_layernorm(const float* x, const float* w, const float* b, int R, int d, __half* out16, float* out32,
                      cudaStream_t st) {
   int ld16 = (d + 7) / 8 * 8;
-  layernorm_kernel<<<(R + 7) / 8, 256, 0, st>>>(x, w, b, R, d, out16, ld16, out32);
+  const unsigned grid = (R + 7) / 8;
+  switch (d) {
+    case 384: layernorm_reg_kernel<3><<<grid, 256, 0, st>>>(x, w, b, R, out16, ld16, out32); break;
+    case 512: layernorm_reg_kernel<4><<<grid, 256, 0, st>>>(x, w, b, R, out16, ld16, out32); break;
+    case 768: layernorm_reg_kernel<6><<<grid, 256, 0, st>>>(x, w, b, R, out16, ld16, out32); break;
+    case 1024: layernorm_reg_kernel<8><<<grid, 256, 0, st>>>(x, w, b, R, out16, ld16, out32); break;
+    case 1280: layernorm_reg_kernel<10><<<grid, 256, 0, st>>>(x, w, b, R, out16, ld16, out32); break;
+    default: layernorm_kernel<<<grid, 256, 0, st>>>(x, w, b, R, d, out16, ld16, out32);
+  }
   return launch_status("layernorm");
 }
 

@@ -166,6 +166,88 @@ __device__ __forceinline__ void epi_store(const Epi& e, int r, int n, float v) {
   }
 }
 
+
+// Output addressing of one weight row n: element (r, n) lives at
+// base + r * row_stride + col_off (CROSS_KV adds the utterance / frame split).
+struct EpiRow {
+  int64_t col_off, row_stride;
+  float bias;
+  int kind;  // 0 f32 store, 1 f32 residual add, 2 f16 GELU, 3 f16 store (K/V cache), 4 cross K/V
+  bool ok;
+};
+
+__device__ __forceinline__ EpiRow epi_row(const Epi& e, int n, int pos) {
+  EpiRow er{0, 0, 0.f, 0, n < e.N};
+  const int nn = er.ok ? n : 0;
+  switch (e.mode) {
+    case EPI_F32: er.kind = 0; er.bias = e.bias ? e.bias[nn] : 0.f; er.col_off = nn; er.row_stride = e.ldo; break;
+    case EPI_RESID: er.kind = 1; er.bias = e.bias ? e.bias[nn] : 0.f; er.col_off = nn; er.row_stride = e.ldo; break;
+    case EPI_GELU_F16: er.kind = 2; er.bias = e.bias ? e.bias[nn] : 0.f; er.col_off = nn; er.row_stride = e.ldo; break;
+    case EPI_QKV: {
+      const int seg = nn / e.d, j = nn - seg * e.d, h = j / e.hd, c = j - h * e.hd;
+      if (seg == 0) { er.kind = 0; er.bias = e.bias_q[j]; er.col_off = j; er.row_stride = e.ldo; }
+      else {
+        er.kind = 3;
+        er.bias = seg == 2 ? e.bias_v[j] : 0.f;
+        er.col_off = (((int64_t)(seg - 1) * e.H + h) * e.T + pos) * e.hd + c;
+        er.row_stride = (int64_t)2 * e.H * e.T * e.hd;
+      }
+      break;
+    }
+    default: {  // EPI_CROSS_KV
+      const int lk = nn / e.d, j = nn - lk * e.d, l = lk >> 1, kv = lk & 1, h = j / e.hd, c = j - h * e.hd;
+      er.kind = 4;
+      er.bias = kv ? e.bias_v[(int64_t)l * e.d + j] : 0.f;
+      er.col_off = (((int64_t)l * e.U * 2 + kv) * e.H + h) * (int64_t)e.T * e.hd + c;
+    }
+  }
+  return er;
+}
+
+__device__ __forceinline__ int64_t epi_index(const Epi& e, const EpiRow& er, int r) {
+  if (er.kind == 4) {
+    const int u = r / e.T, tt = r - u * e.T;
+    return er.col_off + (int64_t)u * 2 * e.H * e.T * e.hd + (int64_t)tt * e.hd;
+  }
+  return (int64_t)r * er.row_stride + er.col_off;
+}
+
+// The 4*NB accumulators of one thread: rows n0 (c = 0,1) and n0 + 8 (c = 2,3),
+// activation rows rbase(nb) + (c & 1). All loads precede all stores.
+template <int NB>
+__device__ __forceinline__ void epi_fragments(const Epi& e, int n0, int rbase0, float (&acc)[NB][4]) {
+  int pos = 0;
+  if (e.mode == EPI_QKV) pos = *e.pos;
+  const EpiRow er0 = epi_row(e, n0, pos), er1 = epi_row(e, n0 + 8, pos);
+  float old[NB][4];
+  if (e.mode == EPI_RESID) {
+#pragma unroll
+    for (int nb = 0; nb < NB; nb++)
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        const EpiRow& er = (c >> 1) ? er1 : er0;
+        const int r = rbase0 + nb * 8 + (c & 1);
+        old[nb][c] = (er.ok && r < e.R) ? e.out[epi_index(e, er, r)] : 0.f;
+      }
+  }
+#pragma unroll
+  for (int nb = 0; nb < NB; nb++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      const EpiRow& er = (c >> 1) ? er1 : er0;
+      const int r = rbase0 + nb * 8 + (c & 1);
+      if (!er.ok || r >= e.R) continue;
+      const float v = __fadd_rn(acc[nb][c], er.bias);
+      const int64_t idx = epi_index(e, er, r);
+      switch (er.kind) {
+        case 0: e.out[idx] = v; break;
+        case 1: e.out[idx] = __fadd_rn(old[nb][c], v); break;
+        case 2: e.out16[idx] = __float2half_rn(ref_gelu(v)); break;
+        default: e.kv[idx] = __float2half_rn(v); break;
+      }
+    }
+}
+
 // ---- small-R kernel ------------------------------------------------------------------
 constexpr int SMALL_WK = 8;  // warps splitting K
 constexpr int SMALL_PF = 4;  // blocks in flight per warp
@@ -194,7 +276,6 @@ __global__ void __launch_bounds__(SMALL_WK * 32)
   for (int nb = 0; nb < NB; nb++)
 #pragma unroll
     for (int c = 0; c < 4; c++) acc[nb][c] = 0.f;
-  const int64_t slot0 = (int64_t)tile * KB;
   for (int j0 = 0;; j0 += SMALL_PF) {
     const int kbase = warp + SMALL_WK * j0;
     if (kbase >= KB) break;
@@ -202,7 +283,7 @@ __global__ void __launch_bounds__(SMALL_WK * 32)
 #pragma unroll
     for (int i = 0; i < SMALL_PF; i++) {
       int kb = kbase + SMALL_WK * i;
-      if (kb < KB) p[i] = load_payload<QT>(W, slot0 + kb, lane);
+      if (kb < KB) p[i] = load_payload<QT>(W, slot_of(W, tile, kb), lane);
     }
 #pragma unroll
     for (int i = 0; i < SMALL_PF; i++) {
@@ -234,13 +315,9 @@ __global__ void __launch_bounds__(SMALL_WK * 32)
 #pragma unroll
   for (int nb = 0; nb < NB; nb++)
 #pragma unroll
-    for (int c = 0; c < 4; c++) {
-      float v = acc[nb][c];
-      for (int w = 1; w < SMALL_WK; w++) v += red[((w * NB + nb) * 4 + c) * 32 + lane];
-      int n = tile * 16 + g + ((c >> 1) << 3);
-      int r = r0 + nb * 8 + 2 * t + (c & 1);
-      if (n < e.N && r < e.R) epi_store(e, r, n, v);
-    }
+    for (int c = 0; c < 4; c++)
+      for (int w = 1; w < SMALL_WK; w++) acc[nb][c] += red[((w * NB + nb) * 4 + c) * 32 + lane];
+  epi_fragments<NB>(e, tile * 16 + g, r0 + 2 * t, acc);
 }
 
 // ---- large-R kernel ------------------------------------------------------------------
@@ -273,8 +350,8 @@ __global__ void __launch_bounds__(128) gemm_large_kernel(DMat W, const __half* _
   for (int nb = 0; nb < LG_NB; nb++)
 #pragma unroll
     for (int c = 0; c < 4; c++) acc[nb][c] = 0.f;
-  const int64_t slot0 = (int64_t)(tile_ok ? tile : 0) * KB;
-  Pay pcur = load_payload<QT>(W, slot0, lane);
+  const int wtile = tile_ok ? tile : 0;
+  Pay pcur = load_payload<QT>(W, slot_of(W, wtile, 0), lane);
   for (int kb = 0; kb < KB; kb++) {
     cp_async_wait<LG_STAGES - 2>();
     __syncthreads();
@@ -282,7 +359,7 @@ __global__ void __launch_bounds__(128) gemm_large_kernel(DMat W, const __half* _
     if (nk < KB) load_stage(nk, nk % LG_STAGES);
     cp_async_commit();
     Pay pnext = pcur;
-    if (kb + 1 < KB) pnext = load_payload<QT>(W, slot0 + kb + 1, lane);
+    if (kb + 1 < KB) pnext = load_payload<QT>(W, slot_of(W, wtile, kb + 1), lane);
     const __half* xb = xs[kb % LG_STAGES];
 #pragma unroll
     for (int s = 0; s < 2; s++) {
@@ -300,14 +377,7 @@ __global__ void __launch_bounds__(128) gemm_large_kernel(DMat W, const __half* _
   }
   cp_async_wait<0>();
   if (!tile_ok) return;
-#pragma unroll
-  for (int nb = 0; nb < LG_NB; nb++)
-#pragma unroll
-    for (int c = 0; c < 4; c++) {
-      int n = tile * 16 + g + ((c >> 1) << 3);
-      int r = r0 + nb * 8 + 2 * t + (c & 1);
-      if (n < e.N && r < e.R) epi_store(e, r, n, acc[nb][c]);
-    }
+  epi_fragments<LG_NB>(e, tile * 16 + g, r0 + 2 * t, acc);
 }
 
 // ---- dense F32 / F16 weights (test-sized models; any K) ----------------------
@@ -350,9 +420,22 @@ int launch_small_t(const DMat& W, const __half* X, int ldx, int R, const Epi& e,
   return launch_status("gemv_small");
 }
 
+// WG_GEMM_LARGE_PATH=2 keeps rows > 16 on the mma.sync kernel (A/B comparisons).
+int large_path_override() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("WG_GEMM_LARGE_PATH");
+    v = (s && *s) ? atoi(s) : 0;
+  }
+  return v;
+}
+
 template <uint32_t QT>
 int launch_q(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st, int path) {
-  if (path == 0) path = R <= 16 ? 1 : (tc_supported(W) ? 3 : 2);
+  if (path == 0) {
+    path = R <= 16 ? 1 : (tc_supported(W) ? 3 : 2);
+    if (path == 3 && large_path_override() == 2) path = 2;
+  }
   if (path == 3) {
     if (!tc_supported(W)) {
       set_error("tcgen05 path needs a quantised matrix with K %% 64 == 0 (K=%d)", W.cols);

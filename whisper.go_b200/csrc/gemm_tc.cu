@@ -10,9 +10,11 @@
 // M = 128 weight rows per CTA and N = NR activation rows (<= 256).
 //
 // Per 64-wide K stage (ring of `stages` buffers, mbarrier handshakes):
-//   warp 4 (one thread): cp.async.bulk of the raw tile16 quant payloads of
-//     the CTA's 8 row tiles -> RAW[s]; TMA 2-D tile load of X[NR, 64] (f16,
-//     128B swizzle) -> B[s]
+//   warp 4 (one thread): cp.async.bulk of the raw quant payloads of the CTA's
+//     128 x 64 weight group (one contiguous run per plane in the tile128
+//     layout) -> RAW[s]
+//   warp 6 (one thread): TMA 2-D tile load of X[NR, 64] (f16, 128B swizzle)
+//     -> B[s]
 //   warps 0-3: dequantise RAW[s] -> A[s] (f16 = d*q rounded once, 128B
 //     swizzled K-major, the same canonical layout TMA writes for B)
 //   warp 5 (one thread): 4 x tcgen05.mma.kind::f16 (K=16) into TMEM, then
@@ -30,7 +32,7 @@ namespace {
 
 constexpr int TC_BM = 128;      // weight rows per CTA (8 tile16 tiles)
 constexpr int TC_BK = 64;       // K per stage
-constexpr int TC_THREADS = 192; // warps 0-3 dequant + epilogue, 4 loader, 5 MMA
+constexpr int TC_THREADS = 224; // warps 0-3 dequant + epilogue, 4 weight loader, 5 MMA, 6 activation loader
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
 
 __device__ int g_tc_error;  // first expired wait: (stage << 8) | role
@@ -117,42 +119,6 @@ __device__ __forceinline__ float tc_gelu(float x) {
   float th = (float)(1.0 + tanh((double)inner));
   return __fmul_rn(__fmul_rn(x, 0.5f), th);
 }
-__device__ __forceinline__ void tc_store(const Epi& e, int r, int n, float v) {
-  switch (e.mode) {
-    case EPI_F32:
-      if (e.bias) v = __fadd_rn(v, e.bias[n]);
-      e.out[(int64_t)r * e.ldo + n] = v;
-      break;
-    case EPI_RESID: {
-      float* p = e.out + (int64_t)r * e.ldo + n;
-      *p = __fadd_rn(*p, __fadd_rn(v, e.bias ? e.bias[n] : 0.f));
-      break;
-    }
-    case EPI_GELU_F16:
-      if (e.bias) v = __fadd_rn(v, e.bias[n]);
-      e.out16[(int64_t)r * e.ldo + n] = __float2half_rn(tc_gelu(v));
-      break;
-    case EPI_QKV: {
-      int seg = n / e.d, j = n - seg * e.d, h = j / e.hd, c = j - h * e.hd;
-      if (seg == 0) {
-        e.out[(int64_t)r * e.ldo + j] = __fadd_rn(v, e.bias_q[j]);
-      } else {
-        if (seg == 2) v = __fadd_rn(v, e.bias_v[j]);
-        int p = *e.pos;
-        e.kv[((((int64_t)r * 2 + (seg - 1)) * e.H + h) * e.T + p) * e.hd + c] = __float2half_rn(v);
-      }
-      break;
-    }
-    case EPI_CROSS_KV: {
-      int u = r / e.T, tt = r - u * e.T;
-      int lk = n / e.d, j = n - lk * e.d, l = lk >> 1, kv = lk & 1, h = j / e.hd, c = j - h * e.hd;
-      if (kv) v = __fadd_rn(v, e.bias_v[(int64_t)l * e.d + j]);
-      e.kv[(((((int64_t)l * e.U + u) * 2 + kv) * e.H + h) * e.T + tt) * e.hd + c] = __float2half_rn(v);
-      break;
-    }
-  }
-}
-
 struct TcLayout {
   int stages;
   uint32_t a_bytes, b_bytes, raw_bytes;
@@ -165,12 +131,12 @@ __host__ __device__ inline TcLayout tc_layout(uint32_t qt, int NR) {
   const int pb = qt == WG_QTYPE_Q8_0 ? 16 : 8;
   L.a_bytes = TC_BM * TC_BK * 2;  // 16 KB
   L.b_bytes = (uint32_t)NR * TC_BK * 2;
-  // RAW: 8 tiles x 2 blocks x { 32 lanes x pb | 8 half2 d | 8 half2 m | 32 u16 hb }
+  // RAW: the 16 slots (8 tiles x 2 blocks) of one weight group, plane by plane
   L.qs_off = 0;
-  L.d_off = 8 * 2 * 32 * pb;
-  L.m_off = L.d_off + 8 * 2 * 32;
-  L.hb_off = L.m_off + 8 * 2 * 32;
-  L.raw_bytes = (L.hb_off + 8 * 2 * 64 + 1023) & ~1023u;
+  L.d_off = 16 * 32 * pb;
+  L.m_off = L.d_off + 16 * 8 * 4;
+  L.hb_off = L.m_off + 16 * 8 * 4;
+  L.raw_bytes = (L.hb_off + 16 * 32 * 2 + 1023) & ~1023u;
   const uint32_t per = L.a_bytes + L.b_bytes + L.raw_bytes;
   L.stages = (int)((220u * 1024u) / per);
   if (L.stages > 6) L.stages = 6;
@@ -234,27 +200,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   if (warp == 4) {
     if (lane == 0) {
-      // ---------------- loader ----------------
+      // ---------------- weight loader ----------------
+      const uint32_t tx = 16 * 32 * pb + 16 * 8 * 4 + (has_m ? 16 * 8 * 4 : 0) + (has_h ? 16 * 32 * 2 : 0);
       for (int k = 0; k < nk; k++) {
         const int s = k % S;
         const uint32_t ph = (uint32_t)(k / S) & 1u;
         if (!mbar_wait(RAW_EMPTY(s), ph ^ 1u, abort_flag, (k << 8) | 1)) break;
-        uint32_t tx = 0;
         const uint32_t raw = base + L.raw0 + s * L.raw_bytes;
-        for (int t = 0; t < 8; t++) {
-          if (tile0 + t >= W.ntiles) break;
-          tx += 2 * 32 * pb + 64 + (has_m ? 64 : 0) + (has_h ? 128 : 0);
-        }
+        const int64_t slot = slot_of(W, tile0, 2 * k);  // first of 16 contiguous slots
         mbar_arrive_tx(RAW_FULL(s), tx);
-        for (int t = 0; t < 8; t++) {
-          const int tile = tile0 + t;
-          if (tile >= W.ntiles) break;
-          const int64_t slot = (int64_t)tile * W.kblocks + 2 * k;
-          bulk_g2s(raw + L.qs_off + t * 2 * 32 * pb, W.qs + slot * 32 * pb, 2 * 32 * pb, RAW_FULL(s));
-          bulk_g2s(raw + L.d_off + t * 64, W.dsc + slot * 8, 64, RAW_FULL(s));
-          if (has_m) bulk_g2s(raw + L.m_off + t * 64, W.msc + slot * 8, 64, RAW_FULL(s));
-          if (has_h) bulk_g2s(raw + L.hb_off + t * 128, W.hb + slot * 32, 128, RAW_FULL(s));
-        }
+        bulk_g2s(raw + L.qs_off, W.qs + slot * 32 * pb, 16 * 32 * pb, RAW_FULL(s));
+        bulk_g2s(raw + L.d_off, W.dsc + slot * 8, 16 * 8 * 4, RAW_FULL(s));
+        if (has_m) bulk_g2s(raw + L.m_off, W.msc + slot * 8, 16 * 8 * 4, RAW_FULL(s));
+        if (has_h) bulk_g2s(raw + L.hb_off, W.hb + slot * 32, 16 * 32 * 2, RAW_FULL(s));
+      }
+    }
+  } else if (warp == 6) {
+    if (lane == 0) {
+      // ---------------- activation loader ----------------
+      for (int k = 0; k < nk; k++) {
+        const int s = k % S;
+        const uint32_t ph = (uint32_t)(k / S) & 1u;
         if (!mbar_wait(AB_EMPTY(s), ph ^ 1u, abort_flag, (k << 8) | 2)) break;
         mbar_arrive_tx(MMA_FULL(s), L.b_bytes);
         tma_2d(base + L.b0 + s * L.b_bytes, &xmap, k * TC_BK, r0, MMA_FULL(s));
@@ -373,7 +339,35 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     done_ok = __all_sync(0xffffffffu, done_ok);
     if (done_ok) {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      // Everything the stores need is read before the first store, so no
+      // load waits behind a store it cannot be proven not to alias.
       const int n = tile0 * 16 + warp * 32 + lane;
+      const bool nok = n < e.N;
+      const int nn = nok ? n : 0;
+      float bias_n = 0.f;
+      int64_t col_off = 0, row_stride = 0;  // output element (r, n) at base + r * row_stride + col_off
+      if (e.mode == EPI_F32 || e.mode == EPI_RESID || e.mode == EPI_GELU_F16) {
+        bias_n = e.bias ? e.bias[nn] : 0.f;
+        col_off = nn;
+        row_stride = e.ldo;
+      } else if (e.mode == EPI_QKV) {
+        const int seg = nn / e.d, j = nn - seg * e.d, h = j / e.hd, c = j - h * e.hd;
+        if (seg == 0) {
+          bias_n = e.bias_q[j];
+          col_off = j;
+          row_stride = e.ldo;
+        } else {
+          bias_n = seg == 2 ? e.bias_v[j] : 0.f;
+          const int p = *e.pos;
+          col_off = (((int64_t)(seg - 1) * e.H + h) * e.T + p) * e.hd + c;
+          row_stride = (int64_t)2 * e.H * e.T * e.hd;
+        }
+      } else {  // EPI_CROSS_KV: r = u*T + t
+        const int lk = nn / e.d, j = nn - lk * e.d, l = lk >> 1, kv = lk & 1, h = j / e.hd, c = j - h * e.hd;
+        bias_n = kv ? e.bias_v[(int64_t)l * e.d + j] : 0.f;
+        col_off = (((int64_t)l * e.U * 2 + kv) * e.H + h) * (int64_t)e.T * e.hd + c;
+      }
+      const bool qkv_q = e.mode == EPI_QKV && nn < e.d;
       for (int c0 = 0; c0 < NR; c0 += 16) {
         uint32_t v[16];
         const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
@@ -383,11 +377,41 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
             : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (n < e.N) {
+        if (!nok) continue;
+        const int rb = r0 + c0;
+        if (e.mode == EPI_RESID) {
+          float old[16];
+#pragma unroll
+          for (int i = 0; i < 16; i++) old[i] = rb + i < R ? e.out[(int64_t)(rb + i) * row_stride + col_off] : 0.f;
+#pragma unroll
+          for (int i = 0; i < 16; i++)
+            if (rb + i < R)
+              e.out[(int64_t)(rb + i) * row_stride + col_off] =
+                  __fadd_rn(old[i], __fadd_rn(__uint_as_float(v[i]), bias_n));
+        } else if (e.mode == EPI_F32 || qkv_q) {
+#pragma unroll
+          for (int i = 0; i < 16; i++)
+            if (rb + i < R) e.out[(int64_t)(rb + i) * row_stride + col_off] = __fadd_rn(__uint_as_float(v[i]), bias_n);
+        } else if (e.mode == EPI_GELU_F16) {
+#pragma unroll
+          for (int i = 0; i < 16; i++)
+            if (rb + i < R)
+              e.out16[(int64_t)(rb + i) * row_stride + col_off] =
+                  __float2half_rn(tc_gelu(__fadd_rn(__uint_as_float(v[i]), bias_n)));
+        } else if (e.mode == EPI_QKV) {
+#pragma unroll
+          for (int i = 0; i < 16; i++)
+            if (rb + i < R)
+              e.kv[(int64_t)(rb + i) * row_stride + col_off] = __float2half_rn(__fadd_rn(__uint_as_float(v[i]), bias_n));
+        } else {  // EPI_CROSS_KV
 #pragma unroll
           for (int i = 0; i < 16; i++) {
-            const int r = r0 + c0 + i;
-            if (r < R) tc_store(e, r, n, __uint_as_float(v[i]));
+            const int r = rb + i;
+            if (r < R) {
+              const int u = r / e.T, tt = r - u * e.T;
+              e.kv[col_off + (int64_t)u * 2 * e.H * e.T * e.hd + (int64_t)tt * e.hd] =
+                  __float2half_rn(__fadd_rn(__uint_as_float(v[i]), bias_n));
+            }
           }
         }
       }

@@ -48,8 +48,7 @@ __global__ void repack_tile16_kernel(uint32_t qtype, const uint8_t* __restrict__
   const QOff off = qoff(qtype);
   const uint8_t* b0 = r0 < rows_part ? raw + (int64_t)r0 * row_bytes + (int64_t)kb * bb : nullptr;
   const uint8_t* b1 = r1 < rows_part ? raw + (int64_t)r1 * row_bytes + (int64_t)kb * bb : nullptr;
-  int64_t dtile = (int64_t)(tile0 + tile);
-  int64_t slot = dtile * kblocks + kb;
+  int64_t slot = slot_of(dst, tile0 + tile, kb);
   if (qtype == WG_QTYPE_Q8_0) {
     uint8_t pay[16];
 #pragma unroll
@@ -105,7 +104,7 @@ __global__ void dequant_tile16_kernel(DMat m, int64_t n_valid, float* __restrict
   int kb = k >> 5, kk = k & 31, s = kk >> 4, kr = kk & 15;
   int t = (kr & 7) >> 1, e = kr & 1, reg = ((kr >> 3) << 1) | hi;
   int lane = g * 4 + t;
-  int64_t slot = (int64_t)tile * m.kblocks + kb;
+  int64_t slot = slot_of(m, tile, kb);
   __half2 dd = m.dsc[slot * 8 + g];
   float d = __half2float(hi ? __high2half(dd) : __low2half(dd));
   float v;
@@ -147,7 +146,7 @@ void free_dmat(DMat& m) {
 
 int64_t dmat_device_bytes(const DMat& m) {
   if (!qtype_is_quant(m.qtype)) return (int64_t)m.rows * m.cols * (m.qtype == WG_QTYPE_F32 ? 4 : 2);
-  int64_t slots = (int64_t)m.ntiles * m.kblocks;
+  int64_t slots = dmat_slots(m);
   int64_t b = slots * 32 * qtype_payload_bytes(m.qtype) + slots * 8 * 4;
   if (qtype_has_min(m.qtype)) b += slots * 8 * 4;
   if (qtype_has_hbits(m.qtype)) b += slots * 32 * 2;
@@ -192,18 +191,27 @@ int upload_matrix(const wg_matrix* const* parts, int nparts, DMat* out, cudaStre
     set_error("upload_matrix: unsupported tensor type %u", m.qtype);
     return WG_ERR_UNSUPPORTED;
   }
-  if (m.cols % 32) {
-    set_error("upload_matrix: quantised matrices need cols %% 32 == 0 (got %d)", m.cols);
+  if (m.cols % 64) {
+    set_error("upload_matrix: quantised matrices need cols %% 64 == 0 (got %d)", m.cols);
     return WG_ERR_UNSUPPORTED;
   }
   m.kblocks = m.cols / 32;
   m.ntiles = (rows + 15) / 16;
-  int64_t slots = (int64_t)m.ntiles * m.kblocks;
+  int64_t slots = dmat_slots(m);
   int pb = qtype_payload_bytes(m.qtype);
+  // padding tiles of the last 128-row group stay zero (scale 0 -> value 0)
   WG_CHECK_CUDA(cudaMalloc(&m.qs, (size_t)slots * 32 * pb));
+  WG_CHECK_CUDA(cudaMemsetAsync(m.qs, 0, (size_t)slots * 32 * pb, st));
   WG_CHECK_CUDA(cudaMalloc(&m.dsc, (size_t)slots * 8 * sizeof(__half2)));
-  if (qtype_has_min(m.qtype)) WG_CHECK_CUDA(cudaMalloc(&m.msc, (size_t)slots * 8 * sizeof(__half2)));
-  if (qtype_has_hbits(m.qtype)) WG_CHECK_CUDA(cudaMalloc(&m.hb, (size_t)slots * 32 * 2));
+  WG_CHECK_CUDA(cudaMemsetAsync(m.dsc, 0, (size_t)slots * 8 * sizeof(__half2), st));
+  if (qtype_has_min(m.qtype)) {
+    WG_CHECK_CUDA(cudaMalloc(&m.msc, (size_t)slots * 8 * sizeof(__half2)));
+    WG_CHECK_CUDA(cudaMemsetAsync(m.msc, 0, (size_t)slots * 8 * sizeof(__half2), st));
+  }
+  if (qtype_has_hbits(m.qtype)) {
+    WG_CHECK_CUDA(cudaMalloc(&m.hb, (size_t)slots * 32 * 2));
+    WG_CHECK_CUDA(cudaMemsetAsync(m.hb, 0, (size_t)slots * 32 * 2, st));
+  }
   int64_t row_bytes = gguf_row_bytes(m.qtype, m.cols);
   size_t max_part = 0;
   for (int i = 0; i < nparts; i++) max_part = std::max(max_part, (size_t)parts[i]->rows * row_bytes);
