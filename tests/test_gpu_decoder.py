@@ -43,6 +43,19 @@ def test_teacher_forced_tiny(tiny, mode):
     assert_logits_close(gpu, ref)
 
 
+@pytest.mark.parametrize("xattn", ["stream", "cluster"])
+def test_teacher_forced_cross_attention_kernels(tiny, xattn, monkeypatch):
+    """Both cross-attention kernels (cluster split / streaming two-pass) on a 2-utterance batch."""
+    m, dec = tiny
+    monkeypatch.setenv("WG_XATTN", xattn)
+    encs = [m.encoder_output(u) for u in (5, 6)]
+    forced = np.random.default_rng(9).integers(0, 50257, size=(2, 4))
+    gpu = dec.teacher_forced_logits(encs, PROMPT, forced, wgdec.MODE_CORRECT)
+    for u in range(2):
+        ref = oracle.teacher_forced(m, encs[u], PROMPT, forced[u], wgdec.MODE_CORRECT, m.n_vocab)
+        assert_logits_close(gpu[:, u, :], ref)
+
+
 def margins_along(m, enc, toks, params, mode):
     """Oracle top-2 margins of the penalised logits along a token sequence."""
     P = len(params.prompt)

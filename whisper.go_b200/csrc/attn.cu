@@ -45,7 +45,7 @@ struct SimtArgs {
   int ldo;
 };
 
-constexpr int SIMT_WARPS = 8;
+constexpr int SIMT_WARPS = 4;
 constexpr int SIMT_UNROLL = 4;  // warp steps whose loads are issued together
 
 __global__ void __launch_bounds__(SIMT_WARPS * 32) attn_simt_kernel(SimtArgs a) {
@@ -429,15 +429,183 @@ __global__ void __launch_bounds__(XA_MAX_WARPS * 32)
     __syncthreads();
   }
   cluster.sync();
-  if (crank == 0) {
-    for (int i = threadIdx.x; i < B * 64; i += blockDim.x) {
-      int row = i >> 6, col = i & 63;
-      float v = 0.f;
-      for (int rk = 0; rk < csize; rk++) v += cluster.map_shared_rank(opart, rk)[row * 64 + col];
-      out16[((int64_t)u * B + row) * ldo + h * 64 + col] = __float2half_rn(v);
-    }
+  // every rank sums (in rank order) and writes its share of the outputs
+  for (int i = crank * blockDim.x + threadIdx.x; i < B * 64; i += csize * blockDim.x) {
+    int row = i >> 6, col = i & 63;
+    float v = 0.f;
+    for (int rk = 0; rk < csize; rk++) v += cluster.map_shared_rank(opart, rk)[row * 64 + col];
+    out16[((int64_t)u * B + row) * ldo + h * 64 + col] = __float2half_rn(v);
   }
   cluster.sync();
+}
+
+// ---------------------------------------------------------------------------
+// Streaming cross-attention for large batches: one CTA per (head, utterance)
+// reads K then V of its 1500 frames exactly once through a cp.async ring.
+// Pass 1 (K chunks): S = (q/8) K^T on mma; scores of the B <= 8 beam rows
+// kept in shared memory. Then the exact row maximum, fastExp, sums and the
+// normalised weights (f16). Pass 2 (V chunks): O = P V on mma.
+// ---------------------------------------------------------------------------
+constexpr int XS_WARPS = 4, XS_CH = 128, XS_NS = 3;
+
+__global__ void __launch_bounds__(XS_WARPS * 32)
+    cross_attn_stream_kernel(const float* __restrict__ q, const __half* __restrict__ kvc, int U, int B, int H, int T,
+                             int Tpad, __half* __restrict__ out16, int ldo) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int h = blockIdx.x, u = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+  const int d = H * 64;
+  const int nch = (T + XS_CH - 1) / XS_CH;
+  const int pst = Tpad + 8;  // padded row stride (halves) of P
+  unsigned char* ring = smem;                                              // XS_NS x 16 KB
+  float* S = reinterpret_cast<float*>(smem + XS_NS * XS_CH * 128);        // [B][Tpad]
+  __half* P = reinterpret_cast<__half*>(S + (size_t)B * Tpad);            // [8][pst]
+  float* red = reinterpret_cast<float*>(P + 8 * pst);                      // [XS_WARPS][8] + [8] + [8]
+  const uint32_t ring_addr = (uint32_t)__cvta_generic_to_shared(ring);
+  const __half* kbase = kvc + ((int64_t)u * 2 * H + h) * (int64_t)T * 64;
+  const __half* vbase = kbase + (int64_t)H * T * 64;
+  auto load_chunk = [&](int c) {  // c < nch: K chunk c; else V chunk c - nch
+    const __half* src = c < nch ? kbase : vbase;
+    const int f0 = (c < nch ? c : c - nch) * XS_CH;
+    const uint32_t dst = ring_addr + (c % XS_NS) * (XS_CH * 128);
+    for (int i = threadIdx.x; i < XS_CH * 8; i += XS_WARPS * 32) {
+      int row = i >> 3, ch = i & 7;
+      int f = f0 + row;
+      int ok = f < T ? 16 : 0;
+      int ff = f < T ? f : T - 1;
+      cp_async16(dst + row * 128 + ((ch ^ (row & 7)) << 4), src + (int64_t)ff * 64 + ch * 8, ok);
+    }
+  };
+  // Q A-fragments (rows 0-7 = beams; rows 8-15 are zero), scaled by 2^-3
+  uint32_t qa[4][2];
+  {
+    const float* q0 = q + ((int64_t)u * B + g) * d + h * 64;
+#pragma unroll
+    for (int ks = 0; ks < 4; ks++) {
+      const int k0 = ks * 16 + 2 * t4;
+      const bool ok = g < B;
+      qa[ks][0] = pack_h2(ok ? q0[k0] * 0.125f : 0.f, ok ? q0[k0 + 1] * 0.125f : 0.f);
+      qa[ks][1] = pack_h2(ok ? q0[k0 + 8] * 0.125f : 0.f, ok ? q0[k0 + 9] * 0.125f : 0.f);
+    }
+  }
+  const int total = 2 * nch;
+#pragma unroll
+  for (int c = 0; c < XS_NS - 1; c++) {
+    if (c < total) load_chunk(c);
+    asm volatile("cp.async.commit_group;\n" ::);
+  }
+  float mx = -INFINITY;  // this lane's running max of row g
+  float oacc[8][4];
+#pragma unroll
+  for (int nd = 0; nd < 8; nd++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) oacc[nd][c] = 0.f;
+  for (int c = 0; c < total; c++) {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(XS_NS - 2));
+    __syncthreads();
+    if (c + XS_NS - 1 < total) load_chunk(c + XS_NS - 1);
+    asm volatile("cp.async.commit_group;\n" ::);
+    const uint32_t st = ring_addr + (c % XS_NS) * (XS_CH * 128);
+    if (c < nch) {
+      // scores of frames f0 + warp*32 .. +31
+      const int fw = c * XS_CH + warp * 32;
+#pragma unroll
+      for (int nb = 0; nb < 4; nb++) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int kp = 0; kp < 2; kp++) {
+          const int row = warp * 32 + nb * 8 + (lane & 7);
+          const int ch = kp * 4 + (lane >> 3);
+          uint32_t b[4];
+          ldsm_x4(b, st + row * 128 + ((ch ^ (row & 7)) << 4));
+          uint32_t a0[4] = {qa[2 * kp][0], 0u, qa[2 * kp][1], 0u};
+          uint32_t a1[4] = {qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u};
+          mma16816(acc, a0, b[0], b[1]);
+          mma16816(acc, a1, b[2], b[3]);
+        }
+        const int f = fw + nb * 8 + 2 * t4;
+        if (g < B) {
+          const float s0 = f < T ? acc[0] : -INFINITY, s1 = f + 1 < T ? acc[1] : -INFINITY;
+          S[(size_t)g * Tpad + f] = s0;
+          S[(size_t)g * Tpad + f + 1] = s1;
+          mx = fmaxf(mx, fmaxf(s0, s1));
+        }
+      }
+    } else {
+      if (c == nch) {
+        // ---- exact softmax over all frames (rows < B) ----
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        if (t4 == 0) red[warp * 8 + g] = mx;
+        __syncthreads();
+        if (threadIdx.x < 8) {
+          float m = red[threadIdx.x];
+          for (int w = 1; w < XS_WARPS; w++) m = fmaxf(m, red[w * 8 + threadIdx.x]);
+          red[XS_WARPS * 8 + threadIdx.x] = m;
+        }
+        __syncthreads();
+        // exponentials and per-row sums: warp w handles rows w, w+4
+        for (int r = warp; r < 8; r += XS_WARPS) {
+          float ssum = 0.f;
+          if (r < B) {
+            const float rm = red[XS_WARPS * 8 + r];
+            for (int f = lane; f < Tpad; f += 32) {
+              float e = f < T ? ref_fast_exp(__fsub_rn(S[(size_t)r * Tpad + f], rm)) : 0.f;
+              S[(size_t)r * Tpad + f] = e;
+              ssum += e;
+            }
+          }
+          ssum = warp_sum(ssum);
+          const float inv = ssum == 0.f ? 0.f : __fdiv_rn(1.f, ssum);
+          for (int f = lane; f < Tpad; f += 32)
+            P[(size_t)r * pst + f] = __float2half_rn(r < B ? __fmul_rn(S[(size_t)r * Tpad + f], inv) : 0.f);
+        }
+        __syncthreads();
+      }
+      // O += P V over frames f0 + warp*32 .. +31 (two k-steps of 16)
+      const int fw = (c - nch) * XS_CH + warp * 32;
+#pragma unroll
+      for (int kk = 0; kk < 2; kk++) {
+        const __half* pr = P + (size_t)g * pst + fw + kk * 16 + 2 * t4;
+        uint32_t pa[4];
+        pa[0] = *reinterpret_cast<const uint32_t*>(pr);
+        pa[1] = 0u;
+        pa[2] = *reinterpret_cast<const uint32_t*>(pr + 8);
+        pa[3] = 0u;
+#pragma unroll
+        for (int ndp = 0; ndp < 4; ndp++) {
+          const int mtx = lane >> 3;
+          const int row = warp * 32 + kk * 16 + (mtx & 1) * 8 + (lane & 7);
+          const int ch = ndp * 2 + (mtx >> 1);
+          uint32_t b[4];
+          ldsm_x4_t(b, st + row * 128 + ((ch ^ (row & 7)) << 4));
+          mma16816(oacc[2 * ndp], pa, b[0], b[1]);
+          mma16816(oacc[2 * ndp + 1], pa, b[2], b[3]);
+        }
+      }
+    }
+  }
+  asm volatile("cp.async.wait_group 0;\n" ::);
+  __syncthreads();
+  // reduce O over the warps (rows g < B), warps in order
+  float* ored = reinterpret_cast<float*>(ring);  // [XS_WARPS][8][64]
+#pragma unroll
+  for (int nd = 0; nd < 8; nd++) {
+    ored[(warp * 8 + g) * 64 + nd * 8 + 2 * t4] = oacc[nd][0];
+    ored[(warp * 8 + g) * 64 + nd * 8 + 2 * t4 + 1] = oacc[nd][1];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < B * 64; i += blockDim.x) {
+    const int row = i >> 6, col = i & 63;
+    float v = ored[row * 64 + col];
+    for (int w = 1; w < XS_WARPS; w++) v += ored[(w * 8 + row) * 64 + col];
+    out16[((int64_t)u * B + row) * ldo + h * 64 + col] = __float2half_rn(v);
+  }
+}
+
+size_t xs_smem(int B, int T) {
+  const int Tpad = (T + XS_CH - 1) / XS_CH * XS_CH;
+  return (size_t)XS_NS * XS_CH * 128 + (size_t)B * Tpad * 4 + (size_t)8 * (Tpad + 8) * 2 + (XS_WARPS * 8 + 16) * 4;
 }
 
 }  // namespace
@@ -471,11 +639,21 @@ static int cross_wpc(int T) {
 int init_attn_attributes() {
   cudaError_t e = cudaFuncSetAttribute(cross_attn_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        XA_MAX_WARPS * 64 * 256 + (32 + XA_MAX_WARPS * 16 + 16 * 64) * 4);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(cross_attn_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
   if (e != cudaSuccess) {
     set_error("cudaFuncSetAttribute(cross_attn): %s", cudaGetErrorString(e));
     return WG_ERR_CUDA;
   }
   return WG_OK;
+}
+
+// WG_XATTN=cluster|stream forces a cross-attention kernel (A/B comparisons
+// and tests); read at every launch, so it also applies to graphs captured
+// while it is set.
+static int xattn_override() {
+  const char* s = getenv("WG_XATTN");
+  return !s ? 0 : (!strcmp(s, "cluster") ? 1 : (!strcmp(s, "stream") ? 2 : 0));
 }
 
 int launch_cross_attn(const CrossAttnArgs& c, cudaStream_t st) {
@@ -499,6 +677,14 @@ int launch_cross_attn(const CrossAttnArgs& c, cudaStream_t st) {
     a.out16 = c.out16;
     a.ldo = ldo;
     return launch_simt(a, c.U * c.B, c.T, st);
+  }
+  const bool stream_ok = c.B <= 8 && xs_smem(c.B, c.T) <= 200 * 1024;
+  const int ov = xattn_override();
+  if (stream_ok && (ov == 2 || (ov == 0 && c.U * c.H >= 2 * 148))) {
+    const int Tpad = (c.T + XS_CH - 1) / XS_CH * XS_CH;
+    cross_attn_stream_kernel<<<dim3(c.H, c.U), XS_WARPS * 32, xs_smem(c.B, c.T), st>>>(c.q, c.kv, c.U, c.B, c.H, c.T,
+                                                                                       Tpad, c.out16, ldo);
+    return launch_status("cross_attn_stream");
   }
   int S = (c.T + 64 * wpc - 1) / (64 * wpc);
   size_t smem = (size_t)wpc * 64 * 256 + (32 + XA_MAX_WARPS * 16 + 16 * 64) * 4;

@@ -213,23 +213,13 @@ __device__ __forceinline__ int64_t epi_index(const Epi& e, const EpiRow& er, int
 }
 
 // The 4*NB accumulators of one thread: rows n0 (c = 0,1) and n0 + 8 (c = 2,3),
-// activation rows rbase(nb) + (c & 1). All loads precede all stores.
+// activation rows rbase(nb) + (c & 1). Residual adds are fire-and-forget
+// reductions, so no store waits on a load.
 template <int NB>
 __device__ __forceinline__ void epi_fragments(const Epi& e, int n0, int rbase0, float (&acc)[NB][4]) {
   int pos = 0;
   if (e.mode == EPI_QKV) pos = *e.pos;
   const EpiRow er0 = epi_row(e, n0, pos), er1 = epi_row(e, n0 + 8, pos);
-  float old[NB][4];
-  if (e.mode == EPI_RESID) {
-#pragma unroll
-    for (int nb = 0; nb < NB; nb++)
-#pragma unroll
-      for (int c = 0; c < 4; c++) {
-        const EpiRow& er = (c >> 1) ? er1 : er0;
-        const int r = rbase0 + nb * 8 + (c & 1);
-        old[nb][c] = (er.ok && r < e.R) ? e.out[epi_index(e, er, r)] : 0.f;
-      }
-  }
 #pragma unroll
   for (int nb = 0; nb < NB; nb++)
 #pragma unroll
@@ -241,7 +231,9 @@ __device__ __forceinline__ void epi_fragments(const Epi& e, int n0, int rbase0, 
       const int64_t idx = epi_index(e, er, r);
       switch (er.kind) {
         case 0: e.out[idx] = v; break;
-        case 1: e.out[idx] = __fadd_rn(old[nb][c], v); break;
+        case 1:  // x += (acc + b); single writer per element
+          asm volatile("red.global.add.f32 [%0], %1;" ::"l"(e.out + idx), "f"(v) : "memory");
+          break;
         case 2: e.out16[idx] = __float2half_rn(ref_gelu(v)); break;
         default: e.kv[idx] = __float2half_rn(v); break;
       }

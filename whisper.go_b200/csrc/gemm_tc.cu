@@ -257,7 +257,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
   } else {
     // ---------------- dequantisers (warps 0-3: row tiles 2w, 2w+1) ----------------
-    const int g = lane >> 2, t = lane & 3;
+    const int g = lane >> 2;
+    // stmatrix row addresses (relative to a stage's A tile): lane l writes row
+    // (l & 7) of 8x8 matrix l >> 3 = (rows +8 if odd, k +8 if >= 2) of each
+    // (tile, block, step) 16x16 fragment, at its 128B-swizzled position
+    uint32_t soff[2][2][2];
+#pragma unroll
+    for (int tt = 0; tt < 2; tt++)
+#pragma unroll
+      for (int blk = 0; blk < 2; blk++)
+#pragma unroll
+        for (int st = 0; st < 2; st++) {
+          const int mtx = lane >> 3;
+          const int row = (warp * 2 + tt) * 16 + (mtx & 1) * 8 + (lane & 7);
+          const int kcol = blk * 32 + st * 16 + (mtx >> 1) * 8;
+          soff[tt][blk][st] = sw128_off(row, kcol);
+        }
     for (int k = 0; k < nk; k++) {
       const int s = k % S;
       const uint32_t ph = (uint32_t)(k / S) & 1u;
@@ -271,7 +286,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
       for (int tt = 0; tt < 2; tt++) {
         const int tl = warp * 2 + tt;
-        const int rowbase = tl * 16;
 #pragma unroll
         for (int blk = 0; blk < 2; blk++) {
           const int sl = tl * 2 + blk;
@@ -318,12 +332,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 a[r] = h2u(v);
               }
             }
-#pragma unroll
-            for (int r = 0; r < 4; r++) {
-              const int row = rowbase + g + 8 * (r & 1);
-              const int kcol = blk * 32 + st * 16 + 8 * (r >> 1) + 2 * t;
-              st_shared_u32(abase + sw128_off(row, kcol), a[r]);
-            }
+            asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(
+                             abase + soff[tt][blk][st]),
+                         "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3])
+                         : "memory");
           }
         }
       }
@@ -380,14 +392,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (!nok) continue;
         const int rb = r0 + c0;
         if (e.mode == EPI_RESID) {
-          float old[16];
-#pragma unroll
-          for (int i = 0; i < 16; i++) old[i] = rb + i < R ? e.out[(int64_t)(rb + i) * row_stride + col_off] : 0.f;
+          // x += (acc + b): one writer per element, so the reduction-add is
+          // deterministic and rounds exactly like the load-add-store
 #pragma unroll
           for (int i = 0; i < 16; i++)
             if (rb + i < R)
-              e.out[(int64_t)(rb + i) * row_stride + col_off] =
-                  __fadd_rn(old[i], __fadd_rn(__uint_as_float(v[i]), bias_n));
+              asm volatile("red.global.add.f32 [%0], %1;" ::"l"(e.out + (int64_t)(rb + i) * row_stride + col_off),
+                           "f"(__fadd_rn(__uint_as_float(v[i]), bias_n))
+                           : "memory");
         } else if (e.mode == EPI_F32 || qkv_q) {
 #pragma unroll
           for (int i = 0; i < 16; i++)
