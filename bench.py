@@ -261,7 +261,11 @@ def main():
         t, b = job.time_kernel(k, iters=3)
         classes[k] = {"ms_per_launch": t, "bytes_per_launch": b, "gbs": b / (t * 1e6) if t > 0 else None,
                       "ms_per_step": t * per_step_launches[k]}
-    dom = max(classes, key=lambda k: classes[k]["ms_per_step"])
+    for k in ("qkv", "self_out", "cross_q", "cross_out", "mlp0", "mlp2", "precompute"):
+        t, b = job.time_kernel(k, iters=3)
+        classes[k] = {"ms_per_launch": t, "bytes_per_launch": b, "gbs": b / (t * 1e6) if t > 0 else None,
+                      "ms_per_step": t * (cfg["L"] if k != "precompute" else 1.0 / max(steps_done, 1))}
+    dom = max(("gemv", "self_attn", "cross_attn", "logits"), key=lambda k: classes[k]["ms_per_step"])
     dk = classes[dom]
     roofline = {"bound": "hbm", "kernel": dom, "achieved": dk["gbs"], "peak": peak, "unit": "GB/s",
                 "frac": dk["gbs"] / peak if dk["gbs"] else None, "traffic": None,

@@ -194,7 +194,14 @@ int wg_matmul_test(uint32_t qtype, const void* raw, int rows, int cols,
                    const float* x, int m, float* out, int path);
 
 /* ---- measurement hooks used by bench.py ---------------------------------- */
-enum { WG_KCLASS_GEMV = 0, WG_KCLASS_SELF_ATTN = 1, WG_KCLASS_CROSS_ATTN = 2, WG_KCLASS_LOGITS = 3 };
+enum {
+  WG_KCLASS_GEMV = 0,        /* the 6 weight matmuls of every layer */
+  WG_KCLASS_SELF_ATTN = 1,
+  WG_KCLASS_CROSS_ATTN = 2,
+  WG_KCLASS_LOGITS = 3,
+  WG_KCLASS_PRECOMPUTE = 4,  /* cross K/V projection of all layers (once per decode) */
+  WG_KCLASS_MATMUL0 = 10     /* + k: only matmul k of {qkv, self out, cross q, cross out, mlp0, mlp2} */
+};
 /* Re-launches one kernel class over all layers of one step on the job's own
  * stream (device 0), iters times, between two CUDA events; *ms = mean time
  * of one launch, *bytes = algorithmic bytes of one launch. Call after

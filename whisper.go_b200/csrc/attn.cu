@@ -446,7 +446,7 @@ __global__ void __launch_bounds__(XA_MAX_WARPS * 32)
 // kept in shared memory. Then the exact row maximum, fastExp, sums and the
 // normalised weights (f16). Pass 2 (V chunks): O = P V on mma.
 // ---------------------------------------------------------------------------
-constexpr int XS_WARPS = 4, XS_CH = 128, XS_NS = 3;
+constexpr int XS_WARPS = 8, XS_CH = 128, XS_NS = 4, XS_FW = XS_CH / XS_WARPS;  // frames per warp per chunk
 
 __global__ void __launch_bounds__(XS_WARPS * 32)
     cross_attn_stream_kernel(const float* __restrict__ q, const __half* __restrict__ kvc, int U, int B, int H, int T,
@@ -459,8 +459,8 @@ __global__ void __launch_bounds__(XS_WARPS * 32)
   const int pst = Tpad + 8;  // padded row stride (halves) of P
   unsigned char* ring = smem;                                              // XS_NS x 16 KB
   float* S = reinterpret_cast<float*>(smem + XS_NS * XS_CH * 128);        // [B][Tpad]
-  __half* P = reinterpret_cast<__half*>(S + (size_t)B * Tpad);            // [8][pst]
-  float* red = reinterpret_cast<float*>(P + 8 * pst);                      // [XS_WARPS][8] + [8] + [8]
+  __half* P = reinterpret_cast<__half*>(S + (size_t)B * Tpad);            // [B][pst]
+  float* red = reinterpret_cast<float*>(P + (size_t)B * pst + (B & 1) * 8); // [XS_WARPS][8] + [8]
   const uint32_t ring_addr = (uint32_t)__cvta_generic_to_shared(ring);
   const __half* kbase = kvc + ((int64_t)u * 2 * H + h) * (int64_t)T * 64;
   const __half* vbase = kbase + (int64_t)H * T * 64;
@@ -507,14 +507,14 @@ __global__ void __launch_bounds__(XS_WARPS * 32)
     asm volatile("cp.async.commit_group;\n" ::);
     const uint32_t st = ring_addr + (c % XS_NS) * (XS_CH * 128);
     if (c < nch) {
-      // scores of frames f0 + warp*32 .. +31
-      const int fw = c * XS_CH + warp * 32;
+      // scores of frames f0 + warp*XS_FW .. +XS_FW-1
+      const int fw = c * XS_CH + warp * XS_FW;
 #pragma unroll
-      for (int nb = 0; nb < 4; nb++) {
+      for (int nb = 0; nb < XS_FW / 8; nb++) {
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int kp = 0; kp < 2; kp++) {
-          const int row = warp * 32 + nb * 8 + (lane & 7);
+          const int row = warp * XS_FW + nb * 8 + (lane & 7);
           const int ch = kp * 4 + (lane >> 3);
           uint32_t b[4];
           ldsm_x4(b, st + row * 128 + ((ch ^ (row & 7)) << 4));
@@ -557,25 +557,25 @@ __global__ void __launch_bounds__(XS_WARPS * 32)
           }
           ssum = warp_sum(ssum);
           const float inv = ssum == 0.f ? 0.f : __fdiv_rn(1.f, ssum);
-          for (int f = lane; f < Tpad; f += 32)
-            P[(size_t)r * pst + f] = __float2half_rn(r < B ? __fmul_rn(S[(size_t)r * Tpad + f], inv) : 0.f);
+          if (r < B)
+            for (int f = lane; f < Tpad; f += 32) P[(size_t)r * pst + f] = __float2half_rn(__fmul_rn(S[(size_t)r * Tpad + f], inv));
         }
         __syncthreads();
       }
-      // O += P V over frames f0 + warp*32 .. +31 (two k-steps of 16)
-      const int fw = (c - nch) * XS_CH + warp * 32;
+      // O += P V over frames f0 + warp*XS_FW .. (k-steps of 16)
+      const int fw = (c - nch) * XS_CH + warp * XS_FW;
 #pragma unroll
-      for (int kk = 0; kk < 2; kk++) {
-        const __half* pr = P + (size_t)g * pst + fw + kk * 16 + 2 * t4;
+      for (int kk = 0; kk < XS_FW / 16; kk++) {
+        const __half* pr = P + (size_t)(g < B ? g : 0) * pst + fw + kk * 16 + 2 * t4;
         uint32_t pa[4];
-        pa[0] = *reinterpret_cast<const uint32_t*>(pr);
+        pa[0] = g < B ? *reinterpret_cast<const uint32_t*>(pr) : 0u;
         pa[1] = 0u;
-        pa[2] = *reinterpret_cast<const uint32_t*>(pr + 8);
+        pa[2] = g < B ? *reinterpret_cast<const uint32_t*>(pr + 8) : 0u;
         pa[3] = 0u;
 #pragma unroll
         for (int ndp = 0; ndp < 4; ndp++) {
           const int mtx = lane >> 3;
-          const int row = warp * 32 + kk * 16 + (mtx & 1) * 8 + (lane & 7);
+          const int row = warp * XS_FW + kk * 16 + (mtx & 1) * 8 + (lane & 7);
           const int ch = ndp * 2 + (mtx >> 1);
           uint32_t b[4];
           ldsm_x4_t(b, st + row * 128 + ((ch ^ (row & 7)) << 4));
@@ -605,7 +605,8 @@ __global__ void __launch_bounds__(XS_WARPS * 32)
 
 size_t xs_smem(int B, int T) {
   const int Tpad = (T + XS_CH - 1) / XS_CH * XS_CH;
-  return (size_t)XS_NS * XS_CH * 128 + (size_t)B * Tpad * 4 + (size_t)8 * (Tpad + 8) * 2 + (XS_WARPS * 8 + 16) * 4;
+  return (size_t)XS_NS * XS_CH * 128 + (size_t)B * Tpad * 4 + (size_t)B * (Tpad + 8) * 2 + 16 +
+         (XS_WARPS * 8 + 16) * 4;
 }
 
 }  // namespace

@@ -132,6 +132,20 @@ __device__ __forceinline__ float ref_fast_exp(float x) {
   return __fmul_rn(poly, __uint_as_float((uint32_t)(k + 127) << 23));
 }
 
+// GELU of internal/ml/ops.go:60-122 (tanh form),
+//   x * 0.5 * (1 + tanh(z)),  z = sqrt(2/pi) * (x + 0.044715 x^3),
+// evaluated through the identity 0.5 * (1 + tanh(z)) = 1 / (1 + exp(-2z)):
+// one exponential and one division instead of a tanh. The reference takes
+// tanh in float64 and rounds 1+tanh to float32; the relative difference of
+// this form (fast exponential and division) is a few 1e-6, far below the
+// float16 rounding of the stored activation, and where exp(-2z) overflows it
+// returns a signed zero (the reference value is then below 1e-30).
+__device__ __forceinline__ float gelu_f32(float x) {
+  const float s2p = 0.7978845608028654f, c = 0.044715f;
+  const float z = s2p * fmaf(c * x, x * x, x);
+  return __fdividef(x, 1.0f + __expf(-2.0f * z));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -987,9 +987,10 @@ int wg_job_time_kernel(wg_job* J, int kclass, int iters, double* ms, double* byt
   auto run = [&](bool count) -> int {
     for (int l = 0; l < L; l++) {
       const DevLayer& ly = dm.layers[l];
-      if (kclass == WG_KCLASS_GEMV) {
+      if (kclass == WG_KCLASS_GEMV || (kclass >= WG_KCLASS_MATMUL0 && kclass < WG_KCLASS_MATMUL0 + 6)) {
         const DMat* mats[6] = {&ly.qkv, &ly.so, &ly.cq, &ly.co, &ly.m0, &ly.m2};
         for (int k = 0; k < 6; k++) {
+          if (kclass != WG_KCLASS_GEMV && k != kclass - WG_KCLASS_MATMUL0) continue;
           Epi e;
           const __half* xin = k == 5 ? j.h16 : (k == 1 || k == 3 ? j.attn16 : j.xln16);
           int ldx = k == 5 ? j.ld4 : j.ldd;
@@ -1020,6 +1021,16 @@ int wg_job_time_kernel(wg_job* J, int kclass, int iters, double* ms, double* byt
         WG_CHECK(launch_cross_attn(ca, j.st));
         if (count) {
           b += (double)j.U * 2 * j.T * d * 2 + (double)R * d * 4 + (double)R * d * 2;
+          launches++;
+        }
+      } else if (kclass == WG_KCLASS_PRECOMPUTE) {
+        if (l > 0) break;
+        Epi e;
+        e.mode = EPI_CROSS_KV; e.kv = j.cross; e.d = d; e.H = H; e.hd = hd; e.T = j.T; e.U = j.U;
+        e.bias_v = dm.cross_vb; e.N = 2 * L * d;
+        WG_CHECK(launch_matmul(dm.cross_kv, j.enc16, j.ldd, j.U * j.T, e, j.st));
+        if (count) {
+          b += (double)dmat_device_bytes(dm.cross_kv) + (double)j.U * j.T * d * 2 + (double)j.U * j.T * 2 * L * d * 2;
           launches++;
         }
       } else if (kclass == WG_KCLASS_LOGITS) {

@@ -122,14 +122,6 @@ __device__ __forceinline__ void dequant_step(const Pay& p, int s, uint32_t* a) {
   }
 }
 
-// GELU of internal/ml/ops.go:102-122 (tanh form, tanh in float64).
-__device__ __forceinline__ float ref_gelu(float x) {
-  const float s2p = 0.7978845608028654f, c = 0.044715f;
-  float inner = __fmul_rn(s2p, __fadd_rn(x, __fmul_rn(__fmul_rn(__fmul_rn(c, x), x), x)));
-  float th = (float)(1.0 + tanh((double)inner));
-  return __fmul_rn(__fmul_rn(x, 0.5f), th);
-}
-
 __device__ __forceinline__ void epi_store(const Epi& e, int r, int n, float v) {
   switch (e.mode) {
     case EPI_F32:
@@ -143,7 +135,7 @@ __device__ __forceinline__ void epi_store(const Epi& e, int r, int n, float v) {
     }
     case EPI_GELU_F16:
       if (e.bias) v = __fadd_rn(v, e.bias[n]);
-      e.out16[(int64_t)r * e.ldo + n] = __float2half_rn(ref_gelu(v));
+      e.out16[(int64_t)r * e.ldo + n] = __float2half_rn(gelu_f32(v));
       break;
     case EPI_QKV: {
       int seg = n / e.d, j = n - seg * e.d, h = j / e.hd, c = j - h * e.hd;
@@ -234,7 +226,7 @@ __device__ __forceinline__ void epi_fragments(const Epi& e, int n0, int rbase0, 
         case 1:  // x += (acc + b); single writer per element
           asm volatile("red.global.add.f32 [%0], %1;" ::"l"(e.out + idx), "f"(v) : "memory");
           break;
-        case 2: e.out16[idx] = __float2half_rn(ref_gelu(v)); break;
+        case 2: e.out16[idx] = __float2half_rn(gelu_f32(v)); break;
         default: e.kv[idx] = __float2half_rn(v); break;
       }
     }

@@ -10,30 +10,45 @@
 // M = 128 weight rows per CTA and N = NR activation rows (<= 256).
 //
 // Per 64-wide K stage (ring of `stages` buffers, mbarrier handshakes):
-//   warp 4 (one thread): cp.async.bulk of the raw quant payloads of the CTA's
-//     128 x 64 weight group (one contiguous run per plane in the tile128
-//     layout) -> RAW[s]
-//   warp 6 (one thread): TMA 2-D tile load of X[NR, 64] (f16, 128B swizzle)
+//   warp 10 (one thread): cp.async.bulk of the raw quant payloads of the
+//     CTA's 128 x 64 weight group (16 contiguous tile128 slots: one copy per
+//     plane) -> RAW[s], a ring of TC_DQ_NS stages
+//   warp 9 (one thread): TMA 2-D tile load of X[NR, 64] (f16, 128B swizzle)
 //     -> B[s]
-//   warps 0-3: dequantise RAW[s] -> A[s] (f16 = d*q rounded once, 128B
-//     swizzled K-major, the same canonical layout TMA writes for B)
-//   warp 5 (one thread): 4 x tcgen05.mma.kind::f16 (K=16) into TMEM, then
+//   warps 0-7: warp w dequantises row tile w of RAW[s] -> A[s] (f16 = d*q
+//     rounded once, stored with stmatrix in the 128B-swizzled K-major
+//     canonical layout TMA writes for B)
+//   warp 8 (one thread): 4 x tcgen05.mma.kind::f16 (K=16) into TMEM, then
 //     tcgen05.commit frees the stage
-//   epilogue: warps 0-3 read their 32 TMEM lanes with tcgen05.ld and apply
-//     the Epi store (bias / residual / GELU / KV-cache scatter).
+// K may be split over a thread-block cluster of ks CTAs (grid z); the
+// epilogue then reduces the partial tiles through distributed shared memory
+// in rank order (deterministic), and stores through the Epi (bias /
+// residual / GELU / KV-cache scatter) with vector accesses.
 // Every mbarrier wait is bounded; on expiry the kernel records an error
 // word, stops waiting and still frees its TMEM.
+#include <cooperative_groups.h>
 #include <cuda.h>
 
+#include <algorithm>
+
 #include "kernels.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace wg {
 namespace {
 
 constexpr int TC_BM = 128;      // weight rows per CTA (8 tile16 tiles)
 constexpr int TC_BK = 64;       // K per stage
-constexpr int TC_THREADS = 224; // warps 0-3 dequant + epilogue, 4 weight loader, 5 MMA, 6 activation loader
-constexpr uint32_t WAIT_LIMIT = 1u << 22;
+constexpr int TC_DQ_WARPS = 16;   // dequantisers (two groups of 8, alternate stages) and TMEM readers
+constexpr int TC_MMA_WARP = 16;   // TMEM owner and MMA issuer
+constexpr int TC_XLOAD_WARP = 17; // activation TMA loader
+constexpr int TC_WLOAD_WARP = 18; // weight bulk-copy loader
+constexpr int TC_THREADS = 19 * 32;
+constexpr int TC_DQ_NS = 6;       // weight stages in flight (raw ring depth)
+constexpr uint32_t WAIT_LIMIT = 1u << 22;      // tries of one bounded wait
+constexpr uint64_t WAIT_NS = 2000000000ull;      // and at most 2 s
+constexpr uint32_t TC_SUSPEND_NS = 100000;       // suspend-time hint of one try
 
 __device__ int g_tc_error;  // first expired wait: (stage << 8) | role
 
@@ -48,23 +63,65 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 __device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t tx) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(tx) : "memory");
 }
+// try_wait with a suspend-time hint: a waiting warp is parked by the
+// hardware until the phase completes (or the hint elapses) instead of
+// spinning, so single-thread producer / MMA warps do not take issue slots
+// from the dequantising warps that share their SM sub-partition.
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(TC_SUSPEND_NS)
       : "memory");
   return ok != 0;
 }
-// Bounded wait: returns false (and raises the CTA abort flag) on expiry.
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait: returns false (and raises the CTA abort flag) once
+// WAIT_LIMIT tries or WAIT_NS nanoseconds have passed, or when another
+// warp of the CTA has aborted.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int code) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
   for (uint32_t i = 0; i < WAIT_LIMIT; i++) {
     if (mbar_try(bar, parity)) return true;
     if (*abort) return false;
+    if (global_ns() - t0 > WAIT_NS) break;
   }
   *abort = 1;
   atomicCAS(&g_tc_error, 0, code);
+  return false;
+}
+
+// Waits for two barriers; both try_waits are issued before either result is
+// used, so their latencies overlap.
+__device__ __forceinline__ bool mbar_wait2(uint32_t bar_a, uint32_t par_a, uint32_t bar_b, uint32_t par_b,
+                                           volatile int* abort, int code) {
+  bool da = false, db = false;
+  uint64_t t0 = 0;
+  for (uint32_t i = 0; i < WAIT_LIMIT; i++) {
+    uint32_t oa, ob;
+    asm volatile(
+        "{\n .reg .pred p, q;\n"
+        " mbarrier.try_wait.parity.shared::cta.b64 p, [%2], %3, %6;\n"
+        " mbarrier.try_wait.parity.shared::cta.b64 q, [%4], %5, %6;\n"
+        " selp.u32 %0, 1, 0, p;\n selp.u32 %1, 1, 0, q;\n}\n"
+        : "=r"(oa), "=r"(ob)
+        : "r"(bar_a), "r"(par_a), "r"(bar_b), "r"(par_b), "r"(TC_SUSPEND_NS)
+        : "memory");
+    da = da || oa != 0;
+    db = db || ob != 0;
+    if (da && db) return true;
+    if (*abort) return false;
+    if (i == 0) t0 = global_ns();
+    else if (global_ns() - t0 > WAIT_NS) break;
+  }
+  *abort = 1;
+  atomicCAS(&g_tc_error, 0, code | (da ? 0 : 0x10) | (db ? 0 : 0x20));
   return false;
 }
 
@@ -92,10 +149,6 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
   return d;
 }
 
-__device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
-  asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
-}
-
 // Byte offset of element (row, k) of a [rows][64] f16 tile in the 128B-swizzled layout.
 __device__ __forceinline__ uint32_t sw128_off(int row, int k) {
   return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
@@ -113,78 +166,188 @@ __device__ __forceinline__ __half2 u2h(uint32_t u) {
 }
 
 // ---- epilogue (shared with gemm.cu's semantics) --------------------------------
-__device__ __forceinline__ float tc_gelu(float x) {
-  const float s2p = 0.7978845608028654f, c = 0.044715f;
-  float inner = __fmul_rn(s2p, __fadd_rn(x, __fmul_rn(__fmul_rn(__fmul_rn(c, x), x), x)));
-  float th = (float)(1.0 + tanh((double)inner));
-  return __fmul_rn(__fmul_rn(x, 0.5f), th);
-}
+// Shared memory: S stages of {A (dequantised weights), B (activation
+// tile)}, as many as fit in 220 KB next to the RAW ring (TC_DQ_NS stages of
+// quant payloads), then the mbarriers.
+constexpr int TC_S_MAX = 6;
 struct TcLayout {
-  int stages;
-  uint32_t a_bytes, b_bytes, raw_bytes;
-  uint32_t qs_off, d_off, m_off, hb_off;  // inside one RAW stage
+  int stages;                    // A/B ring depth
+  uint32_t a_bytes, b_bytes;
+  uint32_t raw_bytes;            // one RAW stage: 16 slots x {32 x pb | d | m | hb}
   uint32_t a0, b0, raw0, bar0, total;
 };
 
 __host__ __device__ inline TcLayout tc_layout(uint32_t qt, int NR) {
   TcLayout L{};
-  const int pb = qt == WG_QTYPE_Q8_0 ? 16 : 8;
   L.a_bytes = TC_BM * TC_BK * 2;  // 16 KB
   L.b_bytes = (uint32_t)NR * TC_BK * 2;
-  // RAW: the 16 slots (8 tiles x 2 blocks) of one weight group, plane by plane
-  L.qs_off = 0;
-  L.d_off = 16 * 32 * pb;
-  L.m_off = L.d_off + 16 * 8 * 4;
-  L.hb_off = L.m_off + 16 * 8 * 4;
-  L.raw_bytes = (L.hb_off + 16 * 32 * 2 + 1023) & ~1023u;
-  const uint32_t per = L.a_bytes + L.b_bytes + L.raw_bytes;
-  L.stages = (int)((220u * 1024u) / per);
-  if (L.stages > 6) L.stages = 6;
+  // d at 16*32*pb, m at +512, hb at +1024 (the m gap is kept when only hb is present)
+  L.raw_bytes = 16 * 32 * qtype_payload_bytes(qt) + 512 + ((qtype_has_min(qt) || qtype_has_hbits(qt)) ? 512 : 0) +
+                (qtype_has_hbits(qt) ? 1024 : 0);
+  const uint32_t raw = TC_DQ_NS * L.raw_bytes;
+  L.stages = (int)((220u * 1024u - raw) / (L.a_bytes + L.b_bytes));
+  if (L.stages > TC_S_MAX) L.stages = TC_S_MAX;
   L.a0 = 0;
   L.b0 = L.a0 + L.stages * L.a_bytes;
   L.raw0 = L.b0 + L.stages * L.b_bytes;
-  L.bar0 = L.raw0 + L.stages * L.raw_bytes;
-  L.total = L.bar0 + 8 * (4 * 6 + 1) + 16 + 1024;  // barriers, tmem slot, alignment slack
+  L.bar0 = L.raw0 + raw;
+  L.total = L.bar0 + 8 * (2 * TC_S_MAX + 2 * TC_DQ_NS + 1) + 16 + 1024;  // barriers, tmem slot, slack
   return L;
 }
 
+// Output addressing of weight row n (fixed per thread in the epilogues):
+// element (r, n) is at base + r * row_stride + col_off, except CROSS_KV whose
+// rows r = u*T + t add u * 2*H*T*hd + t*hd.
+struct TcEpiRow {
+  int64_t col_off, row_stride;
+  float bias;
+  bool ok;
+};
+
+__device__ __forceinline__ TcEpiRow tc_epi_row(const Epi& e, int n) {
+  TcEpiRow er{0, 0, 0.f, n < e.N};
+  const int nn = er.ok ? n : 0;
+  if (e.mode == EPI_F32 || e.mode == EPI_RESID || e.mode == EPI_GELU_F16) {
+    er.bias = e.bias ? e.bias[nn] : 0.f;
+    er.col_off = nn;
+    er.row_stride = e.ldo;
+  } else if (e.mode == EPI_QKV) {
+    const int seg = nn / e.d, j = nn - seg * e.d, h = j / e.hd, c = j - h * e.hd;
+    if (seg == 0) {
+      er.bias = e.bias_q[j];
+      er.col_off = j;
+      er.row_stride = e.ldo;
+    } else {
+      er.bias = seg == 2 ? e.bias_v[j] : 0.f;
+      er.col_off = (((int64_t)(seg - 1) * e.H + h) * e.T + *e.pos) * e.hd + c;
+      er.row_stride = (int64_t)2 * e.H * e.T * e.hd;
+    }
+  } else {  // EPI_CROSS_KV
+    const int lk = nn / e.d, j = nn - lk * e.d, l = lk >> 1, kv = lk & 1, h = j / e.hd, c = j - h * e.hd;
+    er.bias = kv ? e.bias_v[(int64_t)l * e.d + j] : 0.f;
+    er.col_off = (((int64_t)l * e.U * 2 + kv) * e.H + h) * (int64_t)e.T * e.hd + c;
+  }
+  return er;
+}
+
+// Stores acc of rows r0, r0+1, ..., r0+cnt-1 (v[i] for row r0+i) of weight row n.
+template <int CNT>
+__device__ __forceinline__ void tc_epi_store_run(const Epi& e, const TcEpiRow& er, bool qkv_q, int r0, int R,
+                                                 const float* v) {
+  if (e.mode == EPI_CROSS_KV) {
+    int u = r0 / e.T, tt = r0 - u * e.T;  // one division per run
+    const int64_t ustride = (int64_t)2 * e.H * e.T * e.hd;
+#pragma unroll
+    for (int i = 0; i < CNT; i++) {
+      if (r0 + i < R)
+        e.kv[er.col_off + (int64_t)u * ustride + (int64_t)tt * e.hd] = __float2half_rn(__fadd_rn(v[i], er.bias));
+      if (++tt == e.T) { tt = 0; u++; }
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < CNT; i++) {
+    if (r0 + i >= R) break;
+    const float x = __fadd_rn(v[i], er.bias);
+    const int64_t idx = (int64_t)(r0 + i) * er.row_stride + er.col_off;
+    if (e.mode == EPI_RESID) {
+      // x += (acc + b): one writer per element, so the reduction-add is
+      // deterministic and rounds exactly like the load-add-store
+      asm volatile("red.global.add.f32 [%0], %1;" ::"l"(e.out + idx), "f"(x) : "memory");
+    } else if (e.mode == EPI_F32 || qkv_q) {
+      e.out[idx] = x;
+    } else if (e.mode == EPI_GELU_F16) {
+      e.out16[idx] = __float2half_rn(gelu_f32(x));
+    } else {
+      e.kv[idx] = __float2half_rn(x);
+    }
+  }
+}
+
+// Stores x[0..cnt) of weight rows n0..n0+cnt-1 of one activation row, which
+// sit at idx, idx+1, ... of the output: one vector access when all four are
+// valid and the address is aligned. EPI_RESID adds with a vector reduction
+// (one writer per element, so it rounds exactly like load-add-store).
+__device__ __forceinline__ void tc_store_quad(const Epi& e, bool qkv_q, int64_t idx, const float* x, int cnt) {
+  if (e.mode == EPI_RESID || e.mode == EPI_F32 || qkv_q) {
+    float* p = e.out + idx;
+    if (cnt == 4 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+      if (e.mode == EPI_RESID)
+        asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(x[0]), "f"(x[1]), "f"(x[2]),
+                     "f"(x[3])
+                     : "memory");
+      else
+        *reinterpret_cast<float4*>(p) = make_float4(x[0], x[1], x[2], x[3]);
+      return;
+    }
+    for (int i = 0; i < cnt; i++) {
+      if (e.mode == EPI_RESID) asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p + i), "f"(x[i]) : "memory");
+      else p[i] = x[i];
+    }
+    return;
+  }
+  __half* p = (e.mode == EPI_GELU_F16 ? e.out16 : e.kv) + idx;
+  float y[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) y[i] = e.mode == EPI_GELU_F16 ? gelu_f32(x[i]) : x[i];
+  if (cnt == 4 && (reinterpret_cast<uintptr_t>(p) & 7) == 0) {
+    const __half2 h0 = __floats2half2_rn(y[0], y[1]), h1 = __floats2half2_rn(y[2], y[3]);
+    *reinterpret_cast<uint2*>(p) = make_uint2(h2u(h0), h2u(h1));
+    return;
+  }
+  for (int i = 0; i < cnt; i++) p[i] = __float2half_rn(y[i]);
+}
+
+// grid (weight groups, row tiles, K splits); a K split > 1 runs as a thread
+// block cluster along z whose CTAs reduce their partial tiles through
+// distributed shared memory in rank order (deterministic).
 template <uint32_t QT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    gemm_tc_kernel(DMat W, const __grid_constant__ CUtensorMap xmap, int R, int NR, Epi e) {
+    gemm_tc_kernel(DMat W, const __grid_constant__ CUtensorMap xmap, int R, int NR, int ks, Epi e) {
   extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
-  // 1024-byte alignment of the swizzled tiles
   unsigned char* sm = tc_smem_raw + ((1024 - (smem_u32(tc_smem_raw) & 1023)) & 1023);
   const TcLayout L = tc_layout(QT, NR);
   const int S = L.stages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile0 = blockIdx.x * 8;
   const int r0 = blockIdx.y * NR;
-  const int nk = W.cols / TC_BK;
+  const int nk_all = W.cols / TC_BK;
+  const int per = (nk_all + ks - 1) / ks;
+  const int kbeg = blockIdx.z * per;
+  const int nk = min(nk_all, kbeg + per) - kbeg;  // >= 1 (host choice of ks)
+  // CTAs of different weight groups start their K walk at different stages,
+  // so the activation panel they all read is not requested from the same L2
+  // lines by every SM at once
+  const int krot = (int)(blockIdx.x % (unsigned)nk);
+  auto kstage = [&](int kl) { const int k = kl + krot; return kbeg + (k >= nk ? k - nk : k); };
   const uint32_t base = smem_u32(sm);
   const uint32_t bar = base + L.bar0;
-  // barrier groups: raw_full[S], raw_empty[S], mma_full[S], ab_empty[S], done
-  auto RAW_FULL = [&](int s) { return bar + 8 * s; };
-  auto RAW_EMPTY = [&](int s) { return bar + 8 * (6 + s); };
-  auto MMA_FULL = [&](int s) { return bar + 8 * (12 + s); };
-  auto AB_EMPTY = [&](int s) { return bar + 8 * (18 + s); };
-  const uint32_t DONE = bar + 8 * 24;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L.bar0 + 8 * 25);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L.bar0 + 8 * 25 + 4);
+  constexpr int NBAR = 2 * TC_S_MAX + 2 * TC_DQ_NS;
+  // FULL[s]: the stage's dequant group (8 arrivals) + the activation copy
+  // (1 arrival + bytes); EMPTY[s]: the MMAs that read the stage completed
+  auto FULL = [&](int s) { return bar + 8 * s; };
+  auto EMPTY = [&](int s) { return bar + 8 * (TC_S_MAX + s); };
+  auto RAW_FULL = [&](int s) { return bar + 8 * (2 * TC_S_MAX + s); };
+  auto RAW_EMPTY = [&](int s) { return bar + 8 * (2 * TC_S_MAX + TC_DQ_NS + s); };
+  const uint32_t DONE = bar + 8 * NBAR;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L.bar0 + 8 * (NBAR + 1));
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L.bar0 + 8 * (NBAR + 1) + 4);
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; s++) {
+      mbar_init(FULL(s), 8 + 1);
+      mbar_init(EMPTY(s), 1);
+    }
+    for (int s = 0; s < TC_DQ_NS; s++) {
       mbar_init(RAW_FULL(s), 1);
-      mbar_init(RAW_EMPTY(s), 4);
-      mbar_init(MMA_FULL(s), 5);
-      mbar_init(AB_EMPTY(s), 1);
+      mbar_init(RAW_EMPTY(s), 8);
     }
     mbar_init(DONE, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  // TMEM: NR fp32 columns (power of two >= 32)
   uint32_t ncols = 32;
   while (ncols < (uint32_t)NR) ncols <<= 1;
-  if (warp == 5) {
+  if (warp == TC_MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(ncols)
                  : "memory");
@@ -198,240 +361,253 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const bool has_m = QT == WG_QTYPE_Q4_1 || QT == WG_QTYPE_Q5_1;
   const bool has_h = QT == WG_QTYPE_Q5_0 || QT == WG_QTYPE_Q5_1;
 
-  if (warp == 4) {
+  if (warp == TC_WLOAD_WARP) {
     if (lane == 0) {
-      // ---------------- weight loader ----------------
-      const uint32_t tx = 16 * 32 * pb + 16 * 8 * 4 + (has_m ? 16 * 8 * 4 : 0) + (has_h ? 16 * 32 * 2 : 0);
-      for (int k = 0; k < nk; k++) {
-        const int s = k % S;
-        const uint32_t ph = (uint32_t)(k / S) & 1u;
-        if (!mbar_wait(RAW_EMPTY(s), ph ^ 1u, abort_flag, (k << 8) | 1)) break;
-        const uint32_t raw = base + L.raw0 + s * L.raw_bytes;
-        const int64_t slot = slot_of(W, tile0, 2 * k);  // first of 16 contiguous slots
+      // ---------------- weight loader: bulk copies of the stage's 16 contiguous slots ----------------
+      // raw ring slot (per stage): qs [16][32][pb] | d [16][8] half2 | m [16][8] half2 | hb [16][32] u16
+      const uint32_t qs_b = 16 * 32 * pb;
+      const uint32_t tx = qs_b + 512 + (has_m ? 512 : 0) + (has_h ? 1024 : 0);
+      for (int kl = 0; kl < nk; kl++) {
+        const int s = kl % TC_DQ_NS;
+        const uint32_t ph = (uint32_t)(kl / TC_DQ_NS) & 1u;
+        if (!mbar_wait(RAW_EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 1)) break;
+        const uint32_t dst = base + L.raw0 + s * L.raw_bytes;
+        const int64_t g0 = slot_of(W, tile0, 2 * kstage(kl));  // 16 contiguous slots: tile t, blocks 0/1
         mbar_arrive_tx(RAW_FULL(s), tx);
-        bulk_g2s(raw + L.qs_off, W.qs + slot * 32 * pb, 16 * 32 * pb, RAW_FULL(s));
-        bulk_g2s(raw + L.d_off, W.dsc + slot * 8, 16 * 8 * 4, RAW_FULL(s));
-        if (has_m) bulk_g2s(raw + L.m_off, W.msc + slot * 8, 16 * 8 * 4, RAW_FULL(s));
-        if (has_h) bulk_g2s(raw + L.hb_off, W.hb + slot * 32, 16 * 32 * 2, RAW_FULL(s));
+        bulk_g2s(dst, W.qs + g0 * 32 * pb, qs_b, RAW_FULL(s));
+        bulk_g2s(dst + qs_b, W.dsc + g0 * 8, 512, RAW_FULL(s));
+        if (has_m) bulk_g2s(dst + qs_b + 512, W.msc + g0 * 8, 512, RAW_FULL(s));
+        if (has_h) bulk_g2s(dst + qs_b + 1024, W.hb + g0 * 32, 1024, RAW_FULL(s));
       }
     }
-  } else if (warp == 6) {
+  } else if (warp == TC_XLOAD_WARP) {
     if (lane == 0) {
       // ---------------- activation loader ----------------
-      for (int k = 0; k < nk; k++) {
-        const int s = k % S;
-        const uint32_t ph = (uint32_t)(k / S) & 1u;
-        if (!mbar_wait(AB_EMPTY(s), ph ^ 1u, abort_flag, (k << 8) | 2)) break;
-        mbar_arrive_tx(MMA_FULL(s), L.b_bytes);
-        tma_2d(base + L.b0 + s * L.b_bytes, &xmap, k * TC_BK, r0, MMA_FULL(s));
+      for (int kl = 0; kl < nk; kl++) {
+        const int s = kl % S;
+        const uint32_t ph = (uint32_t)(kl / S) & 1u;
+        if (!mbar_wait(EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 2)) break;
+        mbar_arrive_tx(FULL(s), L.b_bytes);
+        tma_2d(base + L.b0 + s * L.b_bytes, &xmap, kstage(kl) * TC_BK, r0, FULL(s));
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == TC_MMA_WARP) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      const uint32_t idesc = (1u << 4)                       // D format: f32
-                             | (0u << 7) | (0u << 10)        // A, B: f16
-                             | ((uint32_t)(NR >> 3) << 17)   // N
+      const uint32_t idesc = (1u << 4)                          // D format: f32
+                             | (0u << 7) | (0u << 10)           // A, B: f16
+                             | ((uint32_t)(NR >> 3) << 17)      // N
                              | ((uint32_t)(TC_BM >> 4) << 24);  // M
-      for (int k = 0; k < nk; k++) {
-        const int s = k % S;
-        const uint32_t ph = (uint32_t)(k / S) & 1u;
-        if (!mbar_wait(MMA_FULL(s), ph, abort_flag, (k << 8) | 3)) break;
+      for (int kl = 0; kl < nk; kl++) {
+        const int s = kl % S;
+        if (!mbar_wait(FULL(s), (uint32_t)(kl / S) & 1u, abort_flag, (kl << 8) | 3)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint64_t ad = sw128_desc(base + L.a0 + s * L.a_bytes);
         const uint64_t bd = sw128_desc(base + L.b0 + s * L.b_bytes);
 #pragma unroll
         for (int kk = 0; kk < 4; kk++) {
-          const uint32_t acc = (k > 0 || kk > 0) ? 1u : 0u;
+          const uint32_t acc = (kl > 0 || kk > 0) ? 1u : 0u;
           asm volatile(
               "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
               " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
               "l"(ad + (uint64_t)(kk * 2)), "l"(bd + (uint64_t)(kk * 2)), "r"(idesc), "r"(acc)
               : "memory");
         }
-        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(AB_EMPTY(s))
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(EMPTY(s))
                      : "memory");
       }
       asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(DONE)
                    : "memory");
     }
   } else {
-    // ---------------- dequantisers (warps 0-3: row tiles 2w, 2w+1) ----------------
-    const int g = lane >> 2;
-    // stmatrix row addresses (relative to a stage's A tile): lane l writes row
-    // (l & 7) of 8x8 matrix l >> 3 = (rows +8 if odd, k +8 if >= 2) of each
-    // (tile, block, step) 16x16 fragment, at its 128B-swizzled position
-    uint32_t soff[2][2][2];
+    // ---------------- dequantisers ----------------
+    // group grp = warp / 8 takes the stages kl = grp (mod 2), so the two
+    // groups' wait / dequantise / fence chains overlap; warp w of a group
+    // owns row tile w (rows 16w..16w+15) of the stage
+    const int g = lane >> 2, grp = warp >> 3, tile = warp & 7;
+    // this warp's two slots (blocks 0/1 of its tile) inside a raw stage
+    const uint32_t d_off = 16 * 32 * pb, m_off = d_off + 512, hb_off = m_off + 512;
+    const unsigned char* rq = sm + L.raw0 + (2 * tile) * 32 * pb;
+    const unsigned char* rd = sm + L.raw0 + d_off + (2 * tile) * 32;
+    const unsigned char* rm = sm + L.raw0 + m_off + (2 * tile) * 32;
+    const unsigned char* rh = sm + L.raw0 + hb_off + (2 * tile) * 64;
+    uint32_t soff[2][2];
 #pragma unroll
-    for (int tt = 0; tt < 2; tt++)
+    for (int blk = 0; blk < 2; blk++)
 #pragma unroll
-      for (int blk = 0; blk < 2; blk++)
-#pragma unroll
-        for (int st = 0; st < 2; st++) {
-          const int mtx = lane >> 3;
-          const int row = (warp * 2 + tt) * 16 + (mtx & 1) * 8 + (lane & 7);
-          const int kcol = blk * 32 + st * 16 + (mtx >> 1) * 8;
-          soff[tt][blk][st] = sw128_off(row, kcol);
-        }
-    for (int k = 0; k < nk; k++) {
-      const int s = k % S;
-      const uint32_t ph = (uint32_t)(k / S) & 1u;
-      bool ok = mbar_wait(RAW_FULL(s), ph, abort_flag, (k << 8) | 4);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok) ok = mbar_wait(AB_EMPTY(s), ph ^ 1u, abort_flag, (k << 8) | 5);
+      for (int st = 0; st < 2; st++) {
+        const int mtx = lane >> 3;
+        soff[blk][st] = sw128_off(tile * 16 + (mtx & 1) * 8 + (lane & 7), blk * 32 + st * 16 + (mtx >> 1) * 8);
+      }
+    for (int kl = grp; kl < nk; kl += 2) {
+      const int s = kl % S;
+      const uint32_t ph = (uint32_t)(kl / S) & 1u;
+      const int rs = kl % TC_DQ_NS;
+      bool ok = mbar_wait2(RAW_FULL(rs), (uint32_t)(kl / TC_DQ_NS) & 1u, EMPTY(s), ph ^ 1u, abort_flag,
+                           (kl << 8) | 4);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
-      const unsigned char* raw = sm + L.raw0 + s * L.raw_bytes;
+      const uint32_t ro = rs * L.raw_bytes;
       const uint32_t abase = base + L.a0 + s * L.a_bytes;
 #pragma unroll
-      for (int tt = 0; tt < 2; tt++) {
-        const int tl = warp * 2 + tt;
+      for (int blk = 0; blk < 2; blk++) {
+        const __half2 dd = reinterpret_cast<const __half2*>(rd + ro)[blk * 8 + g];
+        const __half2 dg = __low2half2(dd), dg8 = __high2half2(dd);
+        __half2 mg = __float2half2_rn(0.f), mg8 = mg;
+        if (has_m) {
+          const __half2 mm = reinterpret_cast<const __half2*>(rm + ro)[blk * 8 + g];
+          mg = __low2half2(mm);
+          mg8 = __high2half2(mm);
+        }
+        uint4 q;
+        uint32_t hb = 0;
+        if (QT == WG_QTYPE_Q8_0) q = reinterpret_cast<const uint4*>(rq + ro)[blk * 32 + lane];
+        else {
+          uint2 v = reinterpret_cast<const uint2*>(rq + ro)[blk * 32 + lane];
+          q = make_uint4(v.x, v.y, 0, 0);
+        }
+        if (has_h) hb = reinterpret_cast<const uint16_t*>(rh + ro)[blk * 32 + lane];
 #pragma unroll
-        for (int blk = 0; blk < 2; blk++) {
-          const int sl = tl * 2 + blk;
-          const __half2 dd = reinterpret_cast<const __half2*>(raw + L.d_off)[sl * 8 + g];
-          const __half2 dg = __low2half2(dd), dg8 = __high2half2(dd);
-          __half2 mg = __float2half2_rn(0.f), mg8 = mg;
-          if (has_m) {
-            const __half2 mm = reinterpret_cast<const __half2*>(raw + L.m_off)[sl * 8 + g];
-            mg = __low2half2(mm);
-            mg8 = __high2half2(mm);
-          }
-          uint4 q;
-          uint32_t hb = 0;
-          if (QT == WG_QTYPE_Q8_0) q = reinterpret_cast<const uint4*>(raw + L.qs_off)[sl * 32 + lane];
-          else {
-            uint2 v = reinterpret_cast<const uint2*>(raw + L.qs_off)[sl * 32 + lane];
-            q = make_uint4(v.x, v.y, 0, 0);
-          }
-          if (has_h) hb = reinterpret_cast<const uint16_t*>(raw + L.hb_off)[sl * 32 + lane];
+        for (int st = 0; st < 2; st++) {
+          uint32_t a[4];
+          if (QT == WG_QTYPE_Q8_0) {
+            uint32_t w0 = (st ? q.z : q.x) ^ 0x80808080u, w1 = (st ? q.w : q.y) ^ 0x80808080u;
+            const __half2 bias = __float2half2_rn(1152.f);
+            a[0] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w0, 0x64, 0x4140)), bias), dg));
+            a[1] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w0, 0x64, 0x4342)), bias), dg8));
+            a[2] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w1, 0x64, 0x4140)), bias), dg));
+            a[3] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w1, 0x64, 0x4342)), bias), dg8));
+          } else {
+            uint32_t w = st ? q.y : q.x;
 #pragma unroll
-          for (int st = 0; st < 2; st++) {
-            uint32_t a[4];
-            if (QT == WG_QTYPE_Q8_0) {
-              uint32_t w0 = (st ? q.z : q.x) ^ 0x80808080u, w1 = (st ? q.w : q.y) ^ 0x80808080u;
-              const __half2 bias = __float2half2_rn(1152.f);
-              a[0] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w0, 0x64, 0x4140)), bias), dg));
-              a[1] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w0, 0x64, 0x4342)), bias), dg8));
-              a[2] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w1, 0x64, 0x4140)), bias), dg));
-              a[3] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w1, 0x64, 0x4342)), bias), dg8));
-            } else {
-              uint32_t w = st ? q.y : q.x;
-#pragma unroll
-              for (int r = 0; r < 4; r++) {
-                uint32_t hq = ((w >> (4 * r)) & 0x000F000Fu) | 0x64006400u;
-                if (has_h) {
-                  uint32_t b = (hb >> (2 * (4 * st + r))) & 3u;
-                  hq |= ((b & 1u) << 4) | ((b >> 1) << 20);
-                }
-                const __half2 d = (r & 1) ? dg8 : dg;
-                __half2 v;
-                if (QT == WG_QTYPE_Q4_0) v = __hmul2(__hsub2(u2h(hq), __float2half2_rn(1032.f)), d);
-                else if (QT == WG_QTYPE_Q5_0) v = __hmul2(__hsub2(u2h(hq), __float2half2_rn(1040.f)), d);
-                else v = __hfma2(__hsub2(u2h(hq), __float2half2_rn(1024.f)), d, (r & 1) ? mg8 : mg);
-                a[r] = h2u(v);
+            for (int r = 0; r < 4; r++) {
+              uint32_t hq = ((w >> (4 * r)) & 0x000F000Fu) | 0x64006400u;
+              if (has_h) {
+                uint32_t b = (hb >> (2 * (4 * st + r))) & 3u;
+                hq |= ((b & 1u) << 4) | ((b >> 1) << 20);
               }
+              const __half2 d = (r & 1) ? dg8 : dg;
+              __half2 v;
+              if (QT == WG_QTYPE_Q4_0) v = __hmul2(__hsub2(u2h(hq), __float2half2_rn(1032.f)), d);
+              else if (QT == WG_QTYPE_Q5_0) v = __hmul2(__hsub2(u2h(hq), __float2half2_rn(1040.f)), d);
+              else v = __hfma2(__hsub2(u2h(hq), __float2half2_rn(1024.f)), d, (r & 1) ? mg8 : mg);
+              a[r] = h2u(v);
             }
-            asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(
-                             abase + soff[tt][blk][st]),
-                         "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3])
-                         : "memory");
           }
+          asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(abase +
+                                                                                                 soff[blk][st]),
+                       "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3])
+                       : "memory");
         }
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(RAW_EMPTY(s));
-        mbar_arrive(MMA_FULL(s));
+        mbar_arrive(RAW_EMPTY(rs));
+        mbar_arrive(FULL(s));
       }
     }
-    // ---------------- epilogue: TMEM lanes 32w..32w+31 ----------------
-    bool done_ok = mbar_wait(DONE, 0, abort_flag, 6);
+  }
+
+  // ---------------- epilogue ----------------
+  // (1) warps 0-7 move the fp32 accumulator tile out of TMEM (warps w and
+  //     w+4 read lanes 32(w%4).. = weight rows of this CTA and split the NR
+  //     columns) into the receive buffer of the cluster rank owning the
+  //     activation row: rcv[k][row - rows_per*owner][128], k = this CTA's
+  //     rank (K split), each owner holding rows_per = ceil(NR / ks) rows.
+  //     Stores to other ranks go through distributed shared memory.
+  // (2) cluster barrier: every partial tile has landed.
+  // (3) all warps: each owner sums its rows over the K splits in rank order
+  //     (deterministic) and applies the Epi store for 4 adjacent weight rows
+  //     per thread, as one 16- or 8-byte vector where the layout allows.
+  // The receive buffer reuses the stage ring; with ks > 1 a first cluster
+  // barrier makes sure no CTA of the cluster still reads its stages.
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = ks > 1 ? (int)cluster.block_rank() : 0;
+  const int rows_per = (NR + ks - 1) / ks;
+  float* rcv = reinterpret_cast<float*>(sm);
+  bool done_ok = true;
+  if (warp < TC_DQ_WARPS) {
+    done_ok = mbar_wait(DONE, 0, abort_flag, 6);
     done_ok = __all_sync(0xffffffffu, done_ok);
-    if (done_ok) {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      // Everything the stores need is read before the first store, so no
-      // load waits behind a store it cannot be proven not to alias.
-      const int n = tile0 * 16 + warp * 32 + lane;
-      const bool nok = n < e.N;
-      const int nn = nok ? n : 0;
-      float bias_n = 0.f;
-      int64_t col_off = 0, row_stride = 0;  // output element (r, n) at base + r * row_stride + col_off
-      if (e.mode == EPI_F32 || e.mode == EPI_RESID || e.mode == EPI_GELU_F16) {
-        bias_n = e.bias ? e.bias[nn] : 0.f;
-        col_off = nn;
-        row_stride = e.ldo;
-      } else if (e.mode == EPI_QKV) {
-        const int seg = nn / e.d, j = nn - seg * e.d, h = j / e.hd, c = j - h * e.hd;
-        if (seg == 0) {
-          bias_n = e.bias_q[j];
-          col_off = j;
-          row_stride = e.ldo;
-        } else {
-          bias_n = seg == 2 ? e.bias_v[j] : 0.f;
-          const int p = *e.pos;
-          col_off = (((int64_t)(seg - 1) * e.H + h) * e.T + p) * e.hd + c;
-          row_stride = (int64_t)2 * e.H * e.T * e.hd;
-        }
-      } else {  // EPI_CROSS_KV: r = u*T + t
-        const int lk = nn / e.d, j = nn - lk * e.d, l = lk >> 1, kv = lk & 1, h = j / e.hd, c = j - h * e.hd;
-        bias_n = kv ? e.bias_v[(int64_t)l * e.d + j] : 0.f;
-        col_off = (((int64_t)l * e.U * 2 + kv) * e.H + h) * (int64_t)e.T * e.hd + c;
-      }
-      const bool qkv_q = e.mode == EPI_QKV && nn < e.d;
-      for (int c0 = 0; c0 < NR; c0 += 16) {
-        uint32_t v[16];
-        const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-            : "r"(taddr));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (!nok) continue;
-        const int rb = r0 + c0;
-        if (e.mode == EPI_RESID) {
-          // x += (acc + b): one writer per element, so the reduction-add is
-          // deterministic and rounds exactly like the load-add-store
+  }
+  if (ks > 1) cluster.sync();
+  if (warp < TC_DQ_WARPS && done_ok) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int f = (warp & 3) * 32 + lane;
+    const int nchunk = NR / 16, part = (nchunk + 3) / 4, sub = warp >> 2;
+    const int cbeg = min(nchunk, sub * part), cend = min(nchunk, cbeg + part);
+    for (int ci = cbeg; ci < cend; ci++) {
+      const int c0 = ci * 16;
+      uint32_t v[16];
+      const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)c0;
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+          : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+            "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+          : "r"(taddr));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      int owner = c0 / rows_per, rem = c0 - owner * rows_per;
+      float* dst = owner == crank ? rcv : cluster.map_shared_rank(rcv, owner);
 #pragma unroll
-          for (int i = 0; i < 16; i++)
-            if (rb + i < R)
-              asm volatile("red.global.add.f32 [%0], %1;" ::"l"(e.out + (int64_t)(rb + i) * row_stride + col_off),
-                           "f"(__fadd_rn(__uint_as_float(v[i]), bias_n))
-                           : "memory");
-        } else if (e.mode == EPI_F32 || qkv_q) {
-#pragma unroll
-          for (int i = 0; i < 16; i++)
-            if (rb + i < R) e.out[(int64_t)(rb + i) * row_stride + col_off] = __fadd_rn(__uint_as_float(v[i]), bias_n);
-        } else if (e.mode == EPI_GELU_F16) {
-#pragma unroll
-          for (int i = 0; i < 16; i++)
-            if (rb + i < R)
-              e.out16[(int64_t)(rb + i) * row_stride + col_off] =
-                  __float2half_rn(tc_gelu(__fadd_rn(__uint_as_float(v[i]), bias_n)));
-        } else if (e.mode == EPI_QKV) {
-#pragma unroll
-          for (int i = 0; i < 16; i++)
-            if (rb + i < R)
-              e.kv[(int64_t)(rb + i) * row_stride + col_off] = __float2half_rn(__fadd_rn(__uint_as_float(v[i]), bias_n));
-        } else {  // EPI_CROSS_KV
-#pragma unroll
-          for (int i = 0; i < 16; i++) {
-            const int r = rb + i;
-            if (r < R) {
-              const int u = r / e.T, tt = r - u * e.T;
-              e.kv[col_off + (int64_t)u * 2 * e.H * e.T * e.hd + (int64_t)tt * e.hd] =
-                  __float2half_rn(__fadd_rn(__uint_as_float(v[i]), bias_n));
-            }
-          }
+      for (int i = 0; i < 16; i++) {
+        dst[((size_t)crank * rows_per + rem) * 128 + f] = __uint_as_float(v[i]);
+        if (++rem == rows_per && i < 15) {
+          rem = 0;
+          owner++;
+          dst = owner == crank ? rcv : cluster.map_shared_rank(rcv, owner);
         }
       }
     }
   }
+  if (ks > 1) cluster.sync();
+  else __syncthreads();
+  if (*abort_flag == 0) {
+    const int n0 = tile0 * 16 + 4 * lane;  // weight rows n0 .. n0+3
+    const int nvalid = max(0, min(4, e.N - n0));
+    const TcEpiRow er = tc_epi_row(e, n0);
+    float b4[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) b4[i] = i < nvalid ? tc_epi_row(e, n0 + i).bias : 0.f;
+    const bool qkv_q = e.mode == EPI_QKV && n0 < e.d;
+    // the 4 weight rows are adjacent in the output unless a head of a
+    // cache layout ends inside the quad
+    const bool contig = (e.mode != EPI_QKV && e.mode != EPI_CROSS_KV) || qkv_q || (e.hd & 3) == 0;
+    const int64_t ustride = (int64_t)2 * e.H * e.T * e.hd;
+    const int row_lo = crank * rows_per, nrows = min(rows_per, NR - row_lo);
+    for (int jr = warp; jr < nrows; jr += TC_THREADS / 32) {
+      const int r = r0 + row_lo + jr;
+      if (r >= R) break;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k = 0; k < ks; k++) {  // rank order
+        const float4 p4 = reinterpret_cast<const float4*>(rcv + ((size_t)k * rows_per + jr) * 128)[lane];
+        acc.x += p4.x;
+        acc.y += p4.y;
+        acc.z += p4.z;
+        acc.w += p4.w;
+      }
+      const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+      if (!contig) {
+        for (int i = 0; i < nvalid; i++)
+          tc_epi_store_run<1>(e, tc_epi_row(e, n0 + i), e.mode == EPI_QKV && n0 + i < e.d, r, R, &a4[i]);
+        continue;
+      }
+      float x[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) x[i] = __fadd_rn(a4[i], b4[i]);
+      int64_t idx;
+      if (e.mode == EPI_CROSS_KV) {
+        const int u = r / e.T, tt = r - u * e.T;
+        idx = er.col_off + (int64_t)u * ustride + (int64_t)tt * e.hd;
+      } else {
+        idx = (int64_t)r * er.row_stride + er.col_off;
+      }
+      tc_store_quad(e, qkv_q, idx, x, nvalid);
+    }
+  }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 5) {
+  if (warp == TC_MMA_WARP) {
     __syncwarp();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
@@ -480,8 +656,65 @@ int launch_tc_t(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cu
     return WG_ERR_CUDA;
   }
   const TcLayout L = tc_layout(QT, NR);
-  dim3 grid((W.ntiles + 7) / 8, (R + NR - 1) / NR);
-  gemm_tc_kernel<QT><<<grid, TC_THREADS, L.total, st>>>(W, map, R, NR, e);
+  const int groups = (W.ntiles + 7) / 8, rtiles = (R + NR - 1) / NR, nk = W.cols / TC_BK;
+  // split K over a cluster (<= 8 CTAs) when the output tiles cannot fill the GPU
+  int ks = 1;
+  if (groups * rtiles < 148) {
+    ks = std::min(8, std::max(1, 148 / (groups * rtiles)));
+    ks = std::min(ks, nk);
+    const int per = (nk + ks - 1) / ks;
+    ks = (nk + per - 1) / per;  // every split gets >= 1 stage
+  }
+  // the epilogue's receive buffer [ks][ceil(NR/ks)][128] fp32 reuses the stage ring
+  while (ks > 1 && (uint32_t)ks * ((NR + ks - 1) / ks) * 512u > L.bar0) ks--;
+  if (ks > 1) {
+    // keep every cluster of the grid co-resident (one wave)
+    static thread_local int cached_dev = -1, cached_nr = -1, cached_ks = -1, cached_max = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    for (; ks > 1; ks--) {
+      int per2 = (nk + ks - 1) / ks;
+      if ((nk + per2 - 1) / per2 != ks) continue;
+      int maxc = 0;
+      if (dev == cached_dev && NR == cached_nr && ks == cached_ks) maxc = cached_max;
+      else {
+        cudaLaunchConfig_t qc = {};
+        qc.gridDim = dim3(groups, rtiles, ks);
+        qc.blockDim = dim3(TC_THREADS, 1, 1);
+        qc.dynamicSmemBytes = L.total;
+        cudaLaunchAttribute qa[1];
+        qa[0].id = cudaLaunchAttributeClusterDimension;
+        qa[0].val.clusterDim.x = 1;
+        qa[0].val.clusterDim.y = 1;
+        qa[0].val.clusterDim.z = ks;
+        qc.attrs = qa;
+        qc.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&maxc, gemm_tc_kernel<QT>, &qc) != cudaSuccess) {
+          cudaGetLastError();
+          maxc = 0;
+        }
+        cached_dev = dev; cached_nr = NR; cached_ks = ks; cached_max = maxc;
+      }
+      if (maxc >= groups * rtiles) break;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(groups, rtiles, ks);
+  cfg.blockDim = dim3(TC_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = L.total;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = ks;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<QT>, W, map, R, NR, ks, e);
+  if (err != cudaSuccess) {
+    set_error("launch of gemm_tc failed: %s", cudaGetErrorString(err));
+    return WG_ERR_CUDA;
+  }
   return launch_status("gemm_tc");
 }
 

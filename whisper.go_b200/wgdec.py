@@ -35,7 +35,8 @@ MODE_CORRECT = 1
 WG_OK = 0
 STATUS = {0: "ok", 1: "invalid", 2: "cuda", 3: "oom", 4: "unsupported", 5: "cancelled", 6: "timeout",
           7: "injected", 8: "no_device", 9: "device_flag"}
-KCLASS = {"gemv": 0, "self_attn": 1, "cross_attn": 2, "logits": 3}
+KCLASS = {"gemv": 0, "self_attn": 1, "cross_attn": 2, "logits": 3, "precompute": 4,
+          "qkv": 10, "self_out": 11, "cross_q": 12, "cross_out": 13, "mlp0": 14, "mlp2": 15}
 
 c_float_p = ctypes.POINTER(ctypes.c_float)
 c_int32_p = ctypes.POINTER(ctypes.c_int32)
