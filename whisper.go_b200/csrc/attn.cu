@@ -16,12 +16,15 @@
 //    accumulate).
 #include <cooperative_groups.h>
 
+#include "async.cuh"
 #include "kernels.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace wg {
 namespace {
+
+__device__ int g_attn_error;  // first expired wait of an attention kernel: (chunk << 8) | role
 
 // ---------------------------------------------------------------------------
 // SIMT attention
@@ -441,41 +444,70 @@ __global__ void __launch_bounds__(XA_MAX_WARPS * 32)
 
 // ---------------------------------------------------------------------------
 // Streaming cross-attention for large batches: one CTA per (head, utterance)
-// reads K then V of its 1500 frames exactly once through a cp.async ring.
-// Pass 1 (K chunks): S = (q/8) K^T on mma; scores of the B <= 8 beam rows
-// kept in shared memory. Then the exact row maximum, fastExp, sums and the
-// normalised weights (f16). Pass 2 (V chunks): O = P V on mma.
+// reads K then V of its encoder frames exactly once. Warp XS_WARPS issues
+// one TMA copy per 128-frame chunk (the 128B-swizzled [128][64] f16 box of
+// the utterance's K or V slab; frames >= T read as zeros) into a ring of
+// XS_NS slots with FULL / EMPTY mbarriers; warps 0..XS_WARPS-1 each own 16
+// frames of every chunk:
+//   pass 1 (K chunks): scores (q/8).k of the B <= 8 beam rows on
+//     mma.m16n8k16, kept in registers (the C fragments of two 8-frame
+//     blocks are the A fragment of the P.V product);
+//   the exact row maximum and the exponential sums are combined across the
+//     warps in shared memory; weights p = e * (1/sum) rounded to f16;
+//   pass 2 (V chunks): O += P V on mma; the warps' partial O are summed in
+//     warp order at the end.
 // ---------------------------------------------------------------------------
-constexpr int XS_WARPS = 8, XS_CH = 128, XS_NS = 4, XS_FW = XS_CH / XS_WARPS;  // frames per warp per chunk
+constexpr int XS_WARPS = 8, XS_CH = 128, XS_NS = 6, XS_FW = XS_CH / XS_WARPS;  // frames per warp per chunk
+constexpr int XS_MAXCH = 12;  // chunks of one pass held in registers: T <= 1536
+constexpr int XS_THREADS = (XS_WARPS + 1) * 32;
 
-__global__ void __launch_bounds__(XS_WARPS * 32)
-    cross_attn_stream_kernel(const float* __restrict__ q, const __half* __restrict__ kvc, int U, int B, int H, int T,
-                             int Tpad, __half* __restrict__ out16, int ldo) {
-  extern __shared__ __align__(128) unsigned char smem[];
+__global__ void __launch_bounds__(XS_THREADS, 2)
+    cross_attn_stream_kernel(const float* __restrict__ q, const __grid_constant__ CUtensorMap kvmap, int B, int H,
+                             int T, __half* __restrict__ out16, int ldo) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int h = blockIdx.x, u = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
   const int d = H * 64;
-  const int nch = (T + XS_CH - 1) / XS_CH;
-  const int pst = Tpad + 8;  // padded row stride (halves) of P
-  unsigned char* ring = smem;                                              // XS_NS x 16 KB
-  float* S = reinterpret_cast<float*>(smem + XS_NS * XS_CH * 128);        // [B][Tpad]
-  __half* P = reinterpret_cast<__half*>(S + (size_t)B * Tpad);            // [B][pst]
-  float* red = reinterpret_cast<float*>(P + (size_t)B * pst + (B & 1) * 8); // [XS_WARPS][8] + [8]
-  const uint32_t ring_addr = (uint32_t)__cvta_generic_to_shared(ring);
-  const __half* kbase = kvc + ((int64_t)u * 2 * H + h) * (int64_t)T * 64;
-  const __half* vbase = kbase + (int64_t)H * T * 64;
-  auto load_chunk = [&](int c) {  // c < nch: K chunk c; else V chunk c - nch
-    const __half* src = c < nch ? kbase : vbase;
-    const int f0 = (c < nch ? c : c - nch) * XS_CH;
-    const uint32_t dst = ring_addr + (c % XS_NS) * (XS_CH * 128);
-    for (int i = threadIdx.x; i < XS_CH * 8; i += XS_WARPS * 32) {
-      int row = i >> 3, ch = i & 7;
-      int f = f0 + row;
-      int ok = f < T ? 16 : 0;
-      int ff = f < T ? f : T - 1;
-      cp_async16(dst + row * 128 + ((ch ^ (row & 7)) << 4), src + (int64_t)ff * 64 + ch * 8, ok);
+  const int nch = (T + XS_CH - 1) / XS_CH;  // <= XS_MAXCH (host check)
+  const int total = 2 * nch;
+  const uint32_t ring = smem_u32(smem);                                       // XS_NS x 16 KB
+  float* red = reinterpret_cast<float*>(smem + XS_NS * XS_CH * 128);         // [2][XS_WARPS][8]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(red + 2 * XS_WARPS * 8);      // FULL[XS_NS], EMPTY[XS_NS]
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * XS_NS);
+  const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * XS_NS;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < XS_NS; s++) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, XS_WARPS);
     }
-  };
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp == XS_WARPS) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      const int kslab = (u * 2) * H + h, vslab = (u * 2 + 1) * H + h;
+      int issued = 0;
+      for (int c = 0; c < total; c++) {
+        const int s = c % XS_NS;
+        // slot s is free once chunk c - XS_NS has been consumed by every warp
+        if (c >= XS_NS && !mbar_wait(empty0 + 8 * s, (uint32_t)(c / XS_NS - 1) & 1u, abort_flag, (c << 8) | 2,
+                                     &g_attn_error))
+          break;
+        mbar_arrive_tx(full0 + 8 * s, XS_CH * 128);
+        tma_3d(ring + s * (XS_CH * 128), &kvmap, 0, (c < nch ? c : c - nch) * XS_CH, c < nch ? kslab : vslab,
+               full0 + 8 * s);
+        issued = c + 1;
+      }
+      if (*abort_flag)  // let the copies in flight land before the CTA exits
+        for (int c = max(0, issued - XS_NS); c < issued; c++)
+          mbar_drain(full0 + 8 * (c % XS_NS), (uint32_t)(c / XS_NS) & 1u);
+    }
+    return;
+  }
+  // ---------------- consumers ----------------
   // Q A-fragments (rows 0-7 = beams; rows 8-15 are zero), scaled by 2^-3
   uint32_t qa[4][2];
   {
@@ -488,29 +520,18 @@ __global__ void __launch_bounds__(XS_WARPS * 32)
       qa[ks][1] = pack_h2(ok ? q0[k0 + 8] * 0.125f : 0.f, ok ? q0[k0 + 9] * 0.125f : 0.f);
     }
   }
-  const int total = 2 * nch;
+  bool live = true;
+  float sc[XS_MAXCH][2][2];  // row g: chunk, 8-frame block, frame pair
+  float mx = -INFINITY;
 #pragma unroll
-  for (int c = 0; c < XS_NS - 1; c++) {
-    if (c < total) load_chunk(c);
-    asm volatile("cp.async.commit_group;\n" ::);
-  }
-  float mx = -INFINITY;  // this lane's running max of row g
-  float oacc[8][4];
-#pragma unroll
-  for (int nd = 0; nd < 8; nd++)
-#pragma unroll
-    for (int c = 0; c < 4; c++) oacc[nd][c] = 0.f;
-  for (int c = 0; c < total; c++) {
-    asm volatile("cp.async.wait_group %0;\n" ::"n"(XS_NS - 2));
-    __syncthreads();
-    if (c + XS_NS - 1 < total) load_chunk(c + XS_NS - 1);
-    asm volatile("cp.async.commit_group;\n" ::);
-    const uint32_t st = ring_addr + (c % XS_NS) * (XS_CH * 128);
+  for (int c = 0; c < XS_MAXCH; c++) {
     if (c < nch) {
-      // scores of frames f0 + warp*XS_FW .. +XS_FW-1
-      const int fw = c * XS_CH + warp * XS_FW;
+      const int s = c % XS_NS;
+      if (live)
+        live = mbar_wait(full0 + 8 * s, (uint32_t)(c / XS_NS) & 1u, abort_flag, (c << 8) | 1, &g_attn_error);
+      const uint32_t st = ring + s * (XS_CH * 128);
 #pragma unroll
-      for (int nb = 0; nb < XS_FW / 8; nb++) {
+      for (int nb = 0; nb < 2; nb++) {
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int kp = 0; kp < 2; kp++) {
@@ -523,79 +544,86 @@ __global__ void __launch_bounds__(XS_WARPS * 32)
           mma16816(acc, a0, b[0], b[1]);
           mma16816(acc, a1, b[2], b[3]);
         }
-        const int f = fw + nb * 8 + 2 * t4;
-        if (g < B) {
-          const float s0 = f < T ? acc[0] : -INFINITY, s1 = f + 1 < T ? acc[1] : -INFINITY;
-          S[(size_t)g * Tpad + f] = s0;
-          S[(size_t)g * Tpad + f + 1] = s1;
-          mx = fmaxf(mx, fmaxf(s0, s1));
-        }
+        const int f = c * XS_CH + warp * XS_FW + nb * 8 + 2 * t4;
+        sc[c][nb][0] = f < T ? acc[0] : -INFINITY;
+        sc[c][nb][1] = f + 1 < T ? acc[1] : -INFINITY;
+        mx = fmaxf(mx, fmaxf(sc[c][nb][0], sc[c][nb][1]));
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty0 + 8 * s);
     } else {
-      if (c == nch) {
-        // ---- exact softmax over all frames (rows < B) ----
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        if (t4 == 0) red[warp * 8 + g] = mx;
-        __syncthreads();
-        if (threadIdx.x < 8) {
-          float m = red[threadIdx.x];
-          for (int w = 1; w < XS_WARPS; w++) m = fmaxf(m, red[w * 8 + threadIdx.x]);
-          red[XS_WARPS * 8 + threadIdx.x] = m;
-        }
-        __syncthreads();
-        // exponentials and per-row sums: warp w handles rows w, w+4
-        for (int r = warp; r < 8; r += XS_WARPS) {
-          float ssum = 0.f;
-          if (r < B) {
-            const float rm = red[XS_WARPS * 8 + r];
-            for (int f = lane; f < Tpad; f += 32) {
-              float e = f < T ? ref_fast_exp(__fsub_rn(S[(size_t)r * Tpad + f], rm)) : 0.f;
-              S[(size_t)r * Tpad + f] = e;
-              ssum += e;
-            }
-          }
-          ssum = warp_sum(ssum);
-          const float inv = ssum == 0.f ? 0.f : __fdiv_rn(1.f, ssum);
-          if (r < B)
-            for (int f = lane; f < Tpad; f += 32) P[(size_t)r * pst + f] = __float2half_rn(__fmul_rn(S[(size_t)r * Tpad + f], inv));
-        }
-        __syncthreads();
-      }
-      // O += P V over frames f0 + warp*XS_FW .. (k-steps of 16)
-      const int fw = (c - nch) * XS_CH + warp * XS_FW;
 #pragma unroll
-      for (int kk = 0; kk < XS_FW / 16; kk++) {
-        const __half* pr = P + (size_t)(g < B ? g : 0) * pst + fw + kk * 16 + 2 * t4;
-        uint32_t pa[4];
-        pa[0] = g < B ? *reinterpret_cast<const uint32_t*>(pr) : 0u;
-        pa[1] = 0u;
-        pa[2] = g < B ? *reinterpret_cast<const uint32_t*>(pr + 8) : 0u;
-        pa[3] = 0u;
-#pragma unroll
-        for (int ndp = 0; ndp < 4; ndp++) {
-          const int mtx = lane >> 3;
-          const int row = warp * XS_FW + kk * 16 + (mtx & 1) * 8 + (lane & 7);
-          const int ch = ndp * 2 + (mtx >> 1);
-          uint32_t b[4];
-          ldsm_x4_t(b, st + row * 128 + ((ch ^ (row & 7)) << 4));
-          mma16816(oacc[2 * ndp], pa, b[0], b[1]);
-          mma16816(oacc[2 * ndp + 1], pa, b[2], b[3]);
-        }
-      }
+      for (int nb = 0; nb < 2; nb++) sc[c][nb][0] = sc[c][nb][1] = -INFINITY;
     }
   }
-  asm volatile("cp.async.wait_group 0;\n" ::);
-  __syncthreads();
-  // reduce O over the warps (rows g < B), warps in order
-  float* ored = reinterpret_cast<float*>(ring);  // [XS_WARPS][8][64]
+  // ---- exact softmax over all frames ----
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  if (t4 == 0) red[warp * 8 + g] = mx;
+  asm volatile("bar.sync 1, %0;" ::"n"(XS_WARPS * 32) : "memory");
+  float m = red[g];
+  for (int w = 1; w < XS_WARPS; w++) m = fmaxf(m, red[w * 8 + g]);
+  float ssum = 0.f;
+#pragma unroll
+  for (int c = 0; c < XS_MAXCH; c++)
+#pragma unroll
+    for (int nb = 0; nb < 2; nb++)
+#pragma unroll
+      for (int i = 0; i < 2; i++) {
+        const float e = ref_fast_exp(__fsub_rn(sc[c][nb][i], m));  // 0 for frames >= T
+        sc[c][nb][i] = e;
+        ssum += e;
+      }
+  ssum += __shfl_xor_sync(0xffffffffu, ssum, 1);
+  ssum += __shfl_xor_sync(0xffffffffu, ssum, 2);
+  if (t4 == 0) red[XS_WARPS * 8 + warp * 8 + g] = ssum;
+  asm volatile("bar.sync 1, %0;" ::"n"(XS_WARPS * 32) : "memory");
+  float tot = 0.f;
+  for (int w = 0; w < XS_WARPS; w++) tot += red[XS_WARPS * 8 + w * 8 + g];
+  const float inv = tot == 0.f ? 0.f : __fdiv_rn(1.f, tot);
+  // ---- O += P V ----
+  float oacc[8][4];
+#pragma unroll
+  for (int nd = 0; nd < 8; nd++)
+#pragma unroll
+    for (int k = 0; k < 4; k++) oacc[nd][k] = 0.f;
+#pragma unroll
+  for (int c = 0; c < XS_MAXCH; c++) {
+    if (c < nch) {
+      const int cc = nch + c, s = cc % XS_NS;
+      if (live)
+        live = mbar_wait(full0 + 8 * s, (uint32_t)(cc / XS_NS) & 1u, abort_flag, (cc << 8) | 1, &g_attn_error);
+      const uint32_t st = ring + s * (XS_CH * 128);
+      uint32_t pa[4];
+      pa[0] = g < B ? pack_h2(__fmul_rn(sc[c][0][0], inv), __fmul_rn(sc[c][0][1], inv)) : 0u;
+      pa[1] = 0u;
+      pa[2] = g < B ? pack_h2(__fmul_rn(sc[c][1][0], inv), __fmul_rn(sc[c][1][1], inv)) : 0u;
+      pa[3] = 0u;
+#pragma unroll
+      for (int ndp = 0; ndp < 4; ndp++) {
+        const int mtx = lane >> 3;
+        const int row = warp * XS_FW + (mtx & 1) * 8 + (lane & 7);
+        const int ch = ndp * 2 + (mtx >> 1);
+        uint32_t b[4];
+        ldsm_x4_t(b, st + row * 128 + ((ch ^ (row & 7)) << 4));
+        mma16816(oacc[2 * ndp], pa, b[0], b[1]);
+        mma16816(oacc[2 * ndp + 1], pa, b[2], b[3]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty0 + 8 * s);
+    }
+  }
+  // reduce O over the warps (rows g < B), warps in order; the ring is free
+  // once every consumer warp has passed its last chunk
+  asm volatile("bar.sync 1, %0;" ::"n"(XS_WARPS * 32) : "memory");
+  float* ored = reinterpret_cast<float*>(smem);  // [XS_WARPS][8][64]
 #pragma unroll
   for (int nd = 0; nd < 8; nd++) {
     ored[(warp * 8 + g) * 64 + nd * 8 + 2 * t4] = oacc[nd][0];
     ored[(warp * 8 + g) * 64 + nd * 8 + 2 * t4 + 1] = oacc[nd][1];
   }
-  __syncthreads();
-  for (int i = threadIdx.x; i < B * 64; i += blockDim.x) {
+  asm volatile("bar.sync 1, %0;" ::"n"(XS_WARPS * 32) : "memory");
+  for (int i = threadIdx.x; i < B * 64; i += XS_WARPS * 32) {
     const int row = i >> 6, col = i & 63;
     float v = ored[row * 64 + col];
     for (int w = 1; w < XS_WARPS; w++) v += ored[(w * 8 + row) * 64 + col];
@@ -603,11 +631,7 @@ __global__ void __launch_bounds__(XS_WARPS * 32)
   }
 }
 
-size_t xs_smem(int B, int T) {
-  const int Tpad = (T + XS_CH - 1) / XS_CH * XS_CH;
-  return (size_t)XS_NS * XS_CH * 128 + (size_t)B * Tpad * 4 + (size_t)B * (Tpad + 8) * 2 + 16 +
-         (XS_WARPS * 8 + 16) * 4;
-}
+size_t xs_smem() { return 1024 + (size_t)XS_NS * XS_CH * 128 + 2 * XS_WARPS * 8 * 4 + 16 * XS_NS + 16; }
 
 }  // namespace
 
@@ -637,11 +661,26 @@ static int cross_wpc(int T) {
   return w < 1 ? 1 : w;
 }
 
+int attn_error_word(int* word, bool clear) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_attn_error, sizeof(int));
+  if (e != cudaSuccess) {
+    set_error("reading the attention error word: %s", cudaGetErrorString(e));
+    return WG_ERR_CUDA;
+  }
+  if (clear && v) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_attn_error, &z, sizeof(int));
+  }
+  *word = v;
+  return WG_OK;
+}
+
 int init_attn_attributes() {
   cudaError_t e = cudaFuncSetAttribute(cross_attn_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        XA_MAX_WARPS * 64 * 256 + (32 + XA_MAX_WARPS * 16 + 16 * 64) * 4);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(cross_attn_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    e = cudaFuncSetAttribute(cross_attn_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xs_smem());
   if (e != cudaSuccess) {
     set_error("cudaFuncSetAttribute(cross_attn): %s", cudaGetErrorString(e));
     return WG_ERR_CUDA;
@@ -679,12 +718,28 @@ int launch_cross_attn(const CrossAttnArgs& c, cudaStream_t st) {
     a.ldo = ldo;
     return launch_simt(a, c.U * c.B, c.T, st);
   }
-  const bool stream_ok = c.B <= 8 && xs_smem(c.B, c.T) <= 200 * 1024;
+  const bool stream_ok = c.B <= 8 && c.T <= XS_MAXCH * XS_CH;
   const int ov = xattn_override();
   if (stream_ok && (ov == 2 || (ov == 0 && c.U * c.H >= 2 * 148))) {
-    const int Tpad = (c.T + XS_CH - 1) / XS_CH * XS_CH;
-    cross_attn_stream_kernel<<<dim3(c.H, c.U), XS_WARPS * 32, xs_smem(c.B, c.T), st>>>(c.q, c.kv, c.U, c.B, c.H, c.T,
-                                                                                       Tpad, c.out16, ldo);
+    // the layer's cache as [U*2*H slabs][T frames][64] f16, box [1][XS_CH][64]
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) {
+      set_error("cuTensorMapEncodeTiled is unavailable");
+      return WG_ERR_CUDA;
+    }
+    CUtensorMap map;
+    cuuint64_t dims[3] = {64, (cuuint64_t)c.T, (cuuint64_t)c.U * 2 * c.H};
+    cuuint64_t strides[2] = {128, (cuuint64_t)c.T * 128};
+    cuuint32_t box[3] = {64, XS_CH, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult cr = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(c.kv), dims, strides, box, es,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) {
+      set_error("cuTensorMapEncodeTiled (cross K/V) failed (%d)", (int)cr);
+      return WG_ERR_CUDA;
+    }
+    cross_attn_stream_kernel<<<dim3(c.H, c.U), XS_THREADS, xs_smem(), st>>>(c.q, map, c.B, c.H, c.T, c.out16, ldo);
     return launch_status("cross_attn_stream");
   }
   int S = (c.T + 64 * wpc - 1) / (64 * wpc);

@@ -121,6 +121,24 @@ int64_t env_i64(const char* name, int64_t dflt) {
 }
 
 // Waits for a stream with the host watchdog deadline (WG_TIMEOUT_MS).
+// Error words of the kernels with bounded waits (current device): a wait
+// that expired means a copy or a peer never arrived; the step's results are
+// not trusted.
+static int check_wait_flags() {
+  int w = 0;
+  WG_CHECK(tc_error_word(&w, true));
+  if (w) {
+    set_error("a tcgen05 kernel's bounded wait expired (code 0x%x)", w);
+    return WG_ERR_DEVICE_FLAG;
+  }
+  WG_CHECK(attn_error_word(&w, true));
+  if (w) {
+    set_error("an attention kernel's bounded wait expired (code 0x%x)", w);
+    return WG_ERR_DEVICE_FLAG;
+  }
+  return WG_OK;
+}
+
 int wait_stream(cudaStream_t st) {
   const int64_t limit_ms = env_i64("WG_TIMEOUT_MS", 600000);
   auto t0 = std::chrono::steady_clock::now();
@@ -687,12 +705,7 @@ static int poll_done(wg_job* J) {
   if (total >= J->U) J->all_done = true;
   for (DevJob* j : J->dj) {
     cudaSetDevice(j->dev);
-    int w = 0;
-    WG_CHECK(tc_error_word(&w, true));
-    if (w) {
-      set_error("a tcgen05 kernel's bounded wait expired (code 0x%x)", w);
-      return WG_ERR_DEVICE_FLAG;
-    }
+    WG_CHECK(check_wait_flags());
   }
   return WG_OK;
 }
@@ -861,6 +874,7 @@ int wg_teacher_forced_logits(wg_model* m, const float* const* enc, int U, int T_
     }
     if (rc == WG_OK) rc = launch_forced_step(j.ss, j.st);
     if (rc == WG_OK) rc = wait_stream(j.st);
+    if (rc == WG_OK) rc = check_wait_flags();
   }
   wg_job_destroy(J);
   return rc;
@@ -955,12 +969,7 @@ int wg_matmul_test(uint32_t qtype, const void* raw, int rows, int cols, const fl
   }
   if (rc == WG_OK) rc = wait_stream(st);
   if (rc == WG_OK) {
-    int w = 0;
-    rc = tc_error_word(&w, true);
-    if (rc == WG_OK && w) {
-      set_error("a tcgen05 kernel's bounded wait expired (code 0x%x)", w);
-      rc = WG_ERR_DEVICE_FLAG;
-    }
+    rc = check_wait_flags();
   }
   cudaFree(dx); cudaFree(dx16); cudaFree(dout);
   free_dmat(dm);

@@ -27,10 +27,10 @@
 // Every mbarrier wait is bounded; on expiry the kernel records an error
 // word, stops waiting and still frees its TMEM.
 #include <cooperative_groups.h>
-#include <cuda.h>
 
 #include <algorithm>
 
+#include "async.cuh"
 #include "kernels.cuh"
 
 namespace cg = cooperative_groups;
@@ -46,97 +46,7 @@ constexpr int TC_XLOAD_WARP = 17; // activation TMA loader
 constexpr int TC_WLOAD_WARP = 18; // weight bulk-copy loader
 constexpr int TC_THREADS = 19 * 32;
 constexpr int TC_DQ_NS = 6;       // weight stages in flight (raw ring depth)
-constexpr uint32_t WAIT_LIMIT = 1u << 22;      // tries of one bounded wait
-constexpr uint64_t WAIT_NS = 2000000000ull;      // and at most 2 s
-constexpr uint32_t TC_SUSPEND_NS = 100000;       // suspend-time hint of one try
-
 __device__ int g_tc_error;  // first expired wait: (stage << 8) | role
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t tx) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(tx) : "memory");
-}
-// try_wait with a suspend-time hint: a waiting warp is parked by the
-// hardware until the phase completes (or the hint elapses) instead of
-// spinning, so single-thread producer / MMA warps do not take issue slots
-// from the dequantising warps that share their SM sub-partition.
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(TC_SUSPEND_NS)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-// Bounded wait: returns false (and raises the CTA abort flag) once
-// WAIT_LIMIT tries or WAIT_NS nanoseconds have passed, or when another
-// warp of the CTA has aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int code) {
-  if (mbar_try(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  for (uint32_t i = 0; i < WAIT_LIMIT; i++) {
-    if (mbar_try(bar, parity)) return true;
-    if (*abort) return false;
-    if (global_ns() - t0 > WAIT_NS) break;
-  }
-  *abort = 1;
-  atomicCAS(&g_tc_error, 0, code);
-  return false;
-}
-
-// Waits for two barriers; both try_waits are issued before either result is
-// used, so their latencies overlap.
-__device__ __forceinline__ bool mbar_wait2(uint32_t bar_a, uint32_t par_a, uint32_t bar_b, uint32_t par_b,
-                                           volatile int* abort, int code) {
-  bool da = false, db = false;
-  uint64_t t0 = 0;
-  for (uint32_t i = 0; i < WAIT_LIMIT; i++) {
-    uint32_t oa, ob;
-    asm volatile(
-        "{\n .reg .pred p, q;\n"
-        " mbarrier.try_wait.parity.shared::cta.b64 p, [%2], %3, %6;\n"
-        " mbarrier.try_wait.parity.shared::cta.b64 q, [%4], %5, %6;\n"
-        " selp.u32 %0, 1, 0, p;\n selp.u32 %1, 1, 0, q;\n}\n"
-        : "=r"(oa), "=r"(ob)
-        : "r"(bar_a), "r"(par_a), "r"(bar_b), "r"(par_b), "r"(TC_SUSPEND_NS)
-        : "memory");
-    da = da || oa != 0;
-    db = db || ob != 0;
-    if (da && db) return true;
-    if (*abort) return false;
-    if (i == 0) t0 = global_ns();
-    else if (global_ns() - t0 > WAIT_NS) break;
-  }
-  *abort = 1;
-  atomicCAS(&g_tc_error, 0, code | (da ? 0 : 0x10) | (db ? 0 : 0x20));
-  return false;
-}
-
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "l"(src), "r"(bytes), "r"(bar)
-               : "memory");
-}
-__device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-          "r"(dst),
-      "l"(map), "r"(x), "r"(y), "r"(bar)
-      : "memory");
-}
 
 // K-major, 128B-swizzled canonical operand (8-row atoms of 1024 B).
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
@@ -370,7 +280,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (int kl = 0; kl < nk; kl++) {
         const int s = kl % TC_DQ_NS;
         const uint32_t ph = (uint32_t)(kl / TC_DQ_NS) & 1u;
-        if (!mbar_wait(RAW_EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 1)) break;
+        if (!mbar_wait(RAW_EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 1, &g_tc_error)) break;
         const uint32_t dst = base + L.raw0 + s * L.raw_bytes;
         const int64_t g0 = slot_of(W, tile0, 2 * kstage(kl));  // 16 contiguous slots: tile t, blocks 0/1
         mbar_arrive_tx(RAW_FULL(s), tx);
@@ -386,7 +296,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (int kl = 0; kl < nk; kl++) {
         const int s = kl % S;
         const uint32_t ph = (uint32_t)(kl / S) & 1u;
-        if (!mbar_wait(EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 2)) break;
+        if (!mbar_wait(EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 2, &g_tc_error)) break;
         mbar_arrive_tx(FULL(s), L.b_bytes);
         tma_2d(base + L.b0 + s * L.b_bytes, &xmap, kstage(kl) * TC_BK, r0, FULL(s));
       }
@@ -400,7 +310,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                              | ((uint32_t)(TC_BM >> 4) << 24);  // M
       for (int kl = 0; kl < nk; kl++) {
         const int s = kl % S;
-        if (!mbar_wait(FULL(s), (uint32_t)(kl / S) & 1u, abort_flag, (kl << 8) | 3)) break;
+        if (!mbar_wait(FULL(s), (uint32_t)(kl / S) & 1u, abort_flag, (kl << 8) | 3, &g_tc_error)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint64_t ad = sw128_desc(base + L.a0 + s * L.a_bytes);
         const uint64_t bd = sw128_desc(base + L.b0 + s * L.b_bytes);
@@ -444,7 +354,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t ph = (uint32_t)(kl / S) & 1u;
       const int rs = kl % TC_DQ_NS;
       bool ok = mbar_wait2(RAW_FULL(rs), (uint32_t)(kl / TC_DQ_NS) & 1u, EMPTY(s), ph ^ 1u, abort_flag,
-                           (kl << 8) | 4);
+                           (kl << 8) | 4, &g_tc_error);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       const uint32_t ro = rs * L.raw_bytes;
@@ -528,7 +438,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   float* rcv = reinterpret_cast<float*>(sm);
   bool done_ok = true;
   if (warp < TC_DQ_WARPS) {
-    done_ok = mbar_wait(DONE, 0, abort_flag, 6);
+    done_ok = mbar_wait(DONE, 0, abort_flag, 6, &g_tc_error);
     done_ok = __all_sync(0xffffffffu, done_ok);
   }
   if (ks > 1) cluster.sync();
@@ -612,24 +522,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
   }
-}
-
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
-  return fn;
 }
 
 template <uint32_t QT>
@@ -729,6 +621,20 @@ int configure_tc_t() {
 }
 
 }  // namespace
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
 
 bool tc_supported(const DMat& W) { return qtype_is_quant(W.qtype) && W.cols % TC_BK == 0; }
 

@@ -77,6 +77,8 @@ struct CrossAttnArgs {
   __half* out16;           // [U*B][d]
 };
 int launch_cross_attn(const CrossAttnArgs& a, cudaStream_t st);
+// First expired bounded wait of an attention kernel on the current device (0: none).
+int attn_error_word(int* word, bool clear);
 int init_attn_attributes();
 
 // ---- sampling (sample.cu) ----------------------------------------------------------
