@@ -38,6 +38,7 @@ CONFIGS = {
     5: dict(name="large-v3-shaped Q8_0 beam5 x64", V=51866, d=1280, L=32, H=20, qtype="Q8_0", beam=5, U=64),
 }
 PROMPT = [50258, 50259, 50357, 50363]
+METRIC = "decoder tokens/s per GPU (large-v3 Q8_0, beam 5); % of HBM roofline"  # BASELINE.json metric
 T_ENC, STEPS_PER_DECODE, SEED = 1500, 224, 20261201
 
 
@@ -54,6 +55,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-steps", type=int, default=2)
+    ap.add_argument("--layers", type=int, default=0,
+                    help="decoder layers (default: the config's); fewer only for small profiler captures")
     return ap.parse_args()
 
 
@@ -64,20 +67,32 @@ def dist_env():
     return rank, world, local
 
 
-class Dist:
-    """torch.distributed plumbing: barrier and max over ranks (no data-path collective)."""
+def utterance_ids(rank, U):
+    """Utterances of one rank: each GPU decodes its own U (weak scaling, no data-path collective)."""
+    return [rank * U + u for u in range(U)]
 
-    def __init__(self, world, local):
+
+class Dist:
+    """torch.distributed plumbing: barrier, max and sum over ranks (timing only;
+    nccl on GPUs, gloo when no CUDA device is visible)."""
+
+    def __init__(self, world, local, backend=None, timeout_s=900):
         self.world = world
         self.pg = None
         if world > 1:
             import datetime
             import torch
             import torch.distributed as td
-            torch.cuda.set_device(local)
-            td.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
-                                  device_id=torch.device("cuda", local))
-            self.td, self.torch, self.local = td, torch, local
+            backend = backend or ("nccl" if torch.cuda.is_available() else "gloo")
+            if backend == "nccl":
+                torch.cuda.set_device(local)
+                td.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s),
+                                      device_id=torch.device("cuda", local))
+                self.device = "cuda:%d" % local
+            else:
+                td.init_process_group("gloo", timeout=datetime.timedelta(seconds=timeout_s))
+                self.device = "cpu"
+            self.td, self.torch = td, torch
             self.pg = True
 
     def barrier(self):
@@ -87,14 +102,14 @@ class Dist:
     def max(self, x):
         if not self.pg:
             return x
-        t = self.torch.tensor([float(x)], device="cuda:%d" % self.local, dtype=self.torch.float64)
+        t = self.torch.tensor([float(x)], device=self.device, dtype=self.torch.float64)
         self.td.all_reduce(t, op=self.td.ReduceOp.MAX)
         return float(t.item())
 
     def sum(self, x):
         if not self.pg:
             return x
-        t = self.torch.tensor([float(x)], device="cuda:%d" % self.local, dtype=self.torch.float64)
+        t = self.torch.tensor([float(x)], device=self.device, dtype=self.torch.float64)
         self.td.all_reduce(t, op=self.td.ReduceOp.SUM)
         return float(t.item())
 
@@ -157,6 +172,12 @@ class Clocks:
                 "power_w_max": max(power) if power else None}
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of each kernel class
+# on the default workload, from the ncu captures summarised under profiles/
+# (None where no capture covers the class)
+TRAFFIC = {}
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -193,7 +214,7 @@ def run_reference(args, cfg, rank, world):
         if i >= args.warmup:
             vals.append(cb)
     v = statistics.median([c["value"] for c in vals])
-    line = {"impl": "reference", "metric": "decoder tokens/s", "value": v, "unit": "tokens/s", "n_gpus": world,
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init weights, N(0,1) encoder)",
             "config": {"workload": "config %d: %s" % (args.config, cfg["name"]), "utterances_per_gpu": U,
@@ -214,6 +235,8 @@ def main():
     import wgdec
     dist = Dist(world, local)
     U = args.utterances or cfg["U"]
+    if args.layers:
+        cfg = dict(cfg, L=args.layers)
     mode = wgdec.MODE_CORRECT if args.mode == "correct" else wgdec.MODE_REF_COMPAT
     model = wgdec.SyntheticModel(cfg["V"], cfg["d"], cfg["H"], cfg["L"], 448, cfg["qtype"], seed=SEED)
     dec = wgdec.WhisperDecoder(model, devices=[local])
@@ -221,8 +244,8 @@ def main():
     import torch
     host = torch.empty((U, T_ENC, cfg["d"]), dtype=torch.float32, pin_memory=True)
     hnp = host.numpy()
-    for u in range(U):
-        hnp[u] = model.encoder_output(rank * U + u, T_ENC)
+    for u, uid in enumerate(utterance_ids(rank, U)):
+        hnp[u] = model.encoder_output(uid, T_ENC)
     encs = [hnp[u] for u in range(U)]
     params = wgdec.DecoderParams(prompt=PROMPT, beam_size=cfg["beam"], max_tokens=args.tokens, mode=mode,
                                  suppress_eot=True)
@@ -268,8 +291,19 @@ def main():
     dom = max(("gemv", "self_attn", "cross_attn", "logits"), key=lambda k: classes[k]["ms_per_step"])
     dk = classes[dom]
     roofline = {"bound": "hbm", "kernel": dom, "achieved": dk["gbs"], "peak": peak, "unit": "GB/s",
-                "frac": dk["gbs"] / peak if dk["gbs"] else None, "traffic": None,
+                "frac": dk["gbs"] / peak if dk["gbs"] else None, "traffic": TRAFFIC.get(dom),
                 "peak_kind": peak_kind, "classes": classes}
+    # the north star's step roofline: quantised weight + KV bytes of one token
+    # step (averaged over the decode) at 8 TB/s, against the measured step time
+    n_tok, P = args.tokens, len(PROMPT)
+    mean_pos = P + (n_tok - 1) / 2.0
+    kv_self = rows * cfg["L"] * 2 * mean_pos * cfg["d"] * 2
+    kv_cross = U * cfg["L"] * 2 * T_ENC * cfg["d"] * 2
+    step_bytes = dec.weight_bytes() + kv_self + kv_cross
+    step_ms = ms_max / args.steps / n_tok
+    step_roofline = {"bytes_per_step": step_bytes, "peak_gbs": 8000.0, "roofline_ms": step_bytes / 8e12 * 1e3,
+                     "measured_ms": step_ms, "frac": (step_bytes / 8e12 * 1e3) / step_ms,
+                     "frac_of_measured_peak": (step_bytes / (peak * 1e6)) / step_ms}
 
     job.close()  # free its KV caches before the end-to-end job allocates its own
     # end to end through the public API: pinned host -> device, decode, tokens back
@@ -301,7 +335,7 @@ def main():
         cpu = cpu_baseline(model, cfg, U, args, 448, os.cpu_count() or 1)
 
     if rank == 0:
-        line = {"metric": "decoder tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16xf16->f32",
                 "data": "synthetic (seeded random-init weights, N(0,1) encoder outputs)",
@@ -310,7 +344,8 @@ def main():
                            "mode": args.mode, "kv_dtype": "f16", "t_enc": T_ENC,
                            "l2": "inputs larger than L2 (per-step KV + weights >> 126 MB)",
                            "parallelism": "dp%d (utterances, no collective)" % world},
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+                "roofline": roofline, "step_roofline": step_roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "clocks": clk,
                 "gpu_launches": int(launches)}
         print(json.dumps(line), flush=True)
     dec.close()
