@@ -52,6 +52,8 @@ constexpr int SIMT_WARPS = 4;
 constexpr int SIMT_UNROLL = 4;  // warp steps whose loads are issued together
 
 __global__ void __launch_bounds__(SIMT_WARPS * 32) attn_simt_kernel(SimtArgs a) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float sm[];  // scores [n] then reduction scratch
   const int r = blockIdx.x, h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -204,8 +206,7 @@ int launch_simt(const SimtArgs& a, int R, int n_max, cudaStream_t st) {
     set_error("attention: %d positions exceed the SIMT kernel's shared memory", n_max);
     return WG_ERR_UNSUPPORTED;
   }
-  attn_simt_kernel<<<dim3(R, a.H), SIMT_WARPS * 32, smem, st>>>(a);
-  return launch_status("attn_simt");
+  return launch_check(launch_k(attn_simt_kernel, dim3(R, a.H), dim3(SIMT_WARPS * 32), smem, st, a), "attn_simt");
 }
 
 // ---------------------------------------------------------------------------
@@ -245,6 +246,8 @@ constexpr int XA_MAX_WARPS = 4;
 __global__ void __launch_bounds__(XA_MAX_WARPS * 32)
     cross_attn_mma_kernel(const float* __restrict__ q, const __half* __restrict__ kvc, int U, int B, int H, int T,
                           int wpc, __half* __restrict__ out16, int ldo) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(128) unsigned char smem[];
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
@@ -464,6 +467,8 @@ constexpr int XS_THREADS = (XS_WARPS + 1) * 32;
 __global__ void __launch_bounds__(XS_THREADS, 2)
     cross_attn_stream_kernel(const float* __restrict__ q, const __grid_constant__ CUtensorMap kvmap, int B, int H,
                              int T, __half* __restrict__ out16, int ldo) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int h = blockIdx.x, u = blockIdx.y;
@@ -739,8 +744,9 @@ int launch_cross_attn(const CrossAttnArgs& c, cudaStream_t st) {
       set_error("cuTensorMapEncodeTiled (cross K/V) failed (%d)", (int)cr);
       return WG_ERR_CUDA;
     }
-    cross_attn_stream_kernel<<<dim3(c.H, c.U), XS_THREADS, xs_smem(), st>>>(c.q, map, c.B, c.H, c.T, c.out16, ldo);
-    return launch_status("cross_attn_stream");
+    return launch_check(launch_k(cross_attn_stream_kernel, dim3(c.H, c.U), dim3(XS_THREADS), xs_smem(), st, c.q, map,
+                                 c.B, c.H, c.T, c.out16, ldo),
+                        "cross_attn_stream");
   }
   int S = (c.T + 64 * wpc - 1) / (64 * wpc);
   size_t smem = (size_t)wpc * 64 * 256 + (32 + XA_MAX_WARPS * 16 + 16 * 64) * 4;
@@ -749,13 +755,15 @@ int launch_cross_attn(const CrossAttnArgs& c, cudaStream_t st) {
   cfg.blockDim = dim3(32 * wpc, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = S;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, cross_attn_mma_kernel, c.q, c.kv, c.U, c.B, c.H, c.T, wpc, c.out16, ldo);
   if (e != cudaSuccess) {
     set_error("launch of cross_attn_mma failed: %s", cudaGetErrorString(e));

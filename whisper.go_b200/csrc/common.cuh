@@ -7,6 +7,8 @@
 #include <atomic>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
+#include <utility>
 
 #include "../../include/wg_decoder.h"
 
@@ -40,6 +42,45 @@ inline void count_launch(int64_t n = 1) { g_launches.fetch_add(n, std::memory_or
 inline int launch_status(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
+    set_error("launch of %s failed: %s", what, cudaGetErrorString(e));
+    return WG_ERR_CUDA;
+  }
+  count_launch();
+  return WG_OK;
+}
+
+// ---- programmatic dependent launch ------------------------------------------
+// Kernels of the token step are launched with programmatic stream
+// serialisation: the next kernel of the stream may be scheduled, and run its
+// prologue, while the current one drains. Each such kernel calls pdl_wait()
+// before its first access to memory an earlier kernel wrote (it returns once
+// every earlier kernel of the stream has completed and its writes are
+// visible) and pdl_trigger() to let its own successor be scheduled.
+// WG_PDL=0 turns the attribute off (plain stream order).
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Status of a launch made with launch_k (counts it when it succeeded).
+inline int launch_check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();
     set_error("launch of %s failed: %s", what, cudaGetErrorString(e));
     return WG_ERR_CUDA;
   }

@@ -23,6 +23,14 @@
 namespace wg {
 
 std::atomic<int64_t> g_launches{0};
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("WG_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 static thread_local std::string t_error;
 
 void set_error(const char* fmt, ...) {

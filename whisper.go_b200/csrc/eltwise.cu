@@ -36,6 +36,8 @@ __device__ __forceinline__ float dmat_elem(const DMat& m, int r, int k) {
 // tensor, which is empty when the embedding is quantised, decoder.go:761-766).
 __global__ void embed_kernel(DMat te, const float* __restrict__ pos_emb, const int* __restrict__ tokens,
                              const int* __restrict__ pos, int pos_offset, int d, float* __restrict__ x) {
+  pdl_trigger();
+  pdl_wait();
   int r = blockIdx.x;
   int tok = tokens[r];
   int p = *pos + pos_offset;
@@ -50,6 +52,8 @@ __global__ void embed_kernel(DMat te, const float* __restrict__ pos_emb, const i
 __global__ void layernorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                  const float* __restrict__ b, int R, int d, __half* __restrict__ out16,
                                  int ld16, float* __restrict__ out32) {
+  pdl_trigger();
+  pdl_wait();
   int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   int lane = threadIdx.x & 31;
   if (r >= R) return;
@@ -79,6 +83,8 @@ template <int NV>
 __global__ void layernorm_reg_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                      const float* __restrict__ b, int R, __half* __restrict__ out16, int ld16,
                                      float* __restrict__ out32) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int d = NV * 128;
   const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -136,23 +142,26 @@ __global__ void f32_to_f16_kernel(const float* __restrict__ in, __half* __restri
 
 int launch_embed(const DMat& te, const float* pos_emb, const int* tokens, const int* pos, int pos_offset, int R,
                  int d, float* x, cudaStream_t st) {
-  embed_kernel<<<R, 256, 0, st>>>(te, pos_emb, tokens, pos, pos_offset, d, x);
-  return launch_status("embed");
+  return launch_check(launch_k(embed_kernel, dim3(R), dim3(256), 0, st, te, pos_emb, tokens, pos, pos_offset, d, x),
+                      "embed");
 }
 
 int launch_layernorm(const float* x, const float* w, const float* b, int R, int d, __half* out16, float* out32,
                      cudaStream_t st) {
   int ld16 = (d + 7) / 8 * 8;
   const unsigned grid = (R + 7) / 8;
+  cudaError_t e;
   switch (d) {
-    case 384: layernorm_reg_kernel<3><<<grid, 256, 0, st>>>(x, w, b, R, out16, ld16, out32); break;
-    case 512: layernorm_reg_kernel<4><<<grid, 256, 0, st>>>(x, w, b, R, out16, ld16, out32); break;
-    case 768: layernorm_reg_kernel<6><<<grid, 256, 0, st>>>(x, w, b, R, out16, ld16, out32); break;
-    case 1024: layernorm_reg_kernel<8><<<grid, 256, 0, st>>>(x, w, b, R, out16, ld16, out32); break;
-    case 1280: layernorm_reg_kernel<10><<<grid, 256, 0, st>>>(x, w, b, R, out16, ld16, out32); break;
-    default: layernorm_kernel<<<grid, 256, 0, st>>>(x, w, b, R, d, out16, ld16, out32);
+    case 384: e = launch_k(layernorm_reg_kernel<3>, dim3(grid), dim3(256), 0, st, x, w, b, R, out16, ld16, out32); break;
+    case 512: e = launch_k(layernorm_reg_kernel<4>, dim3(grid), dim3(256), 0, st, x, w, b, R, out16, ld16, out32); break;
+    case 768: e = launch_k(layernorm_reg_kernel<6>, dim3(grid), dim3(256), 0, st, x, w, b, R, out16, ld16, out32); break;
+    case 1024: e = launch_k(layernorm_reg_kernel<8>, dim3(grid), dim3(256), 0, st, x, w, b, R, out16, ld16, out32); break;
+    case 1280:
+      e = launch_k(layernorm_reg_kernel<10>, dim3(grid), dim3(256), 0, st, x, w, b, R, out16, ld16, out32);
+      break;
+    default: e = launch_k(layernorm_kernel, dim3(grid), dim3(256), 0, st, x, w, b, R, d, out16, ld16, out32);
   }
-  return launch_status("layernorm");
+  return launch_check(e, "layernorm");
 }
 
 int launch_f32_to_f16(const float* in, __half* out, int64_t n, cudaStream_t st) {

@@ -239,6 +239,8 @@ constexpr int SMALL_PF = 4;  // blocks in flight per warp
 template <uint32_t QT, int NB>
 __global__ void __launch_bounds__(SMALL_WK * 32)
     gemv_small_kernel(DMat W, const __half* __restrict__ X, int ldx, Epi e) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char smem[];
   constexpr int RC = NB * 8;
   const int K = W.cols, KB = W.kblocks;
@@ -309,6 +311,8 @@ constexpr int LG_RC = 64, LG_NB = 8, LG_STAGES = 4, LG_XS = 40;
 
 template <uint32_t QT>
 __global__ void __launch_bounds__(128) gemm_large_kernel(DMat W, const __half* __restrict__ X, int ldx, Epi e) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ __align__(16) __half xs[LG_STAGES][LG_RC * LG_XS];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int tile = blockIdx.x * 4 + warp;
@@ -368,6 +372,8 @@ __global__ void __launch_bounds__(128) gemm_large_kernel(DMat W, const __half* _
 template <typename WT>
 __global__ void __launch_bounds__(256) gemv_dense_kernel(const WT* __restrict__ W, int N, int K,
                                                           const __half* __restrict__ X, int ldx, Epi e) {
+  pdl_trigger();
+  pdl_wait();
   int n = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (n >= N) return;
   const WT* w = W + (int64_t)n * K;
@@ -400,8 +406,8 @@ int launch_small_t(const DMat& W, const __half* X, int ldx, int R, const Epi& e,
     return WG_ERR_UNSUPPORTED;
   }
   dim3 grid(W.ntiles, (R + RC - 1) / RC);
-  gemv_small_kernel<QT, NB><<<grid, SMALL_WK * 32, smem, st>>>(W, X, ldx, e);
-  return launch_status("gemv_small");
+  return launch_check(launch_k(gemv_small_kernel<QT, NB>, grid, dim3(SMALL_WK * 32), smem, st, W, X, ldx, e),
+                      "gemv_small");
 }
 
 // WG_GEMM_LARGE_PATH=2 keeps rows > 16 on the mma.sync kernel (A/B comparisons).
@@ -434,8 +440,7 @@ int launch_q(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaS
     return launch_small_t<QT, 2>(W, X, ldx, R, e, st);
   }
   dim3 grid((W.ntiles + 3) / 4, (R + LG_RC - 1) / LG_RC);
-  gemm_large_kernel<QT><<<grid, 128, 0, st>>>(W, X, ldx, e);
-  return launch_status("gemm_large");
+  return launch_check(launch_k(gemm_large_kernel<QT>, grid, dim3(128), 0, st, W, X, ldx, e), "gemm_large");
 }
 
 }  // namespace
@@ -472,13 +477,13 @@ int launch_matmul(const DMat& W, const __half* X, int ldx, int R, const Epi& e_i
     case WG_QTYPE_Q5_0: return launch_q<WG_QTYPE_Q5_0>(W, X, ldx, R, e, st, path);
     case WG_QTYPE_Q5_1: return launch_q<WG_QTYPE_Q5_1>(W, X, ldx, R, e, st, path);
     case WG_QTYPE_F32:
-      gemv_dense_kernel<float><<<(W.rows + 7) / 8, 256, 0, st>>>(reinterpret_cast<const float*>(W.qs), W.rows,
-                                                                  W.cols, X, ldx, e);
-      return launch_status("gemv_dense_f32");
+      return launch_check(launch_k(gemv_dense_kernel<float>, dim3((W.rows + 7) / 8), dim3(256), 0, st,
+                                   reinterpret_cast<const float*>(W.qs), W.rows, W.cols, X, ldx, e),
+                          "gemv_dense_f32");
     case WG_QTYPE_F16:
-      gemv_dense_kernel<__half><<<(W.rows + 7) / 8, 256, 0, st>>>(reinterpret_cast<const __half*>(W.qs), W.rows,
-                                                                   W.cols, X, ldx, e);
-      return launch_status("gemv_dense_f16");
+      return launch_check(launch_k(gemv_dense_kernel<__half>, dim3((W.rows + 7) / 8), dim3(256), 0, st,
+                                   reinterpret_cast<const __half*>(W.qs), W.rows, W.cols, X, ldx, e),
+                          "gemv_dense_f16");
     default:
       set_error("launch_matmul: unsupported tensor type %u", W.qtype);
       return WG_ERR_UNSUPPORTED;

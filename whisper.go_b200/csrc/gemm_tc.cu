@@ -216,6 +216,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(DMat W, const __grid_constant__ CUtensorMap xmap, int R, int NR, int ks, Epi e) {
   extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
   unsigned char* sm = tc_smem_raw + ((1024 - (smem_u32(tc_smem_raw) & 1023)) & 1023);
+  // the next kernel of the stream may be scheduled now; this one waits for
+  // its predecessors (pdl_wait) only where it reads activations or writes
+  // outputs: barrier set-up, TMEM allocation and the weight stream (weights
+  // are never written by kernels of the token loop) run before that
+  pdl_trigger();
   const TcLayout L = tc_layout(QT, NR);
   const int S = L.stages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -293,6 +298,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else if (warp == TC_XLOAD_WARP) {
     if (lane == 0) {
       // ---------------- activation loader ----------------
+      pdl_wait();
       for (int kl = 0; kl < nk; kl++) {
         const int s = kl % S;
         const uint32_t ph = (uint32_t)(kl / S) & 1u;
@@ -432,6 +438,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   //     per thread, as one 16- or 8-byte vector where the layout allows.
   // The receive buffer reuses the stage ring; with ks > 1 a first cluster
   // barrier makes sure no CTA of the cluster still reads its stages.
+  pdl_wait();  // (returned long ago for the activation loader)
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = ks > 1 ? (int)cluster.block_rank() : 0;
   const int rows_per = (NR + ks - 1) / ks;
@@ -595,13 +602,15 @@ int launch_tc_t(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cu
   cfg.blockDim = dim3(TC_THREADS, 1, 1);
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = ks;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   cudaError_t err = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<QT>, W, map, R, NR, ks, e);
   if (err != cudaSuccess) {
     set_error("launch of gemm_tc failed: %s", cudaGetErrorString(err));

@@ -15,6 +15,8 @@ namespace {
 
 // ---- repetition penalty: logit[id] -= 2.0 * count(id in last 128 tokens) ----
 __global__ void penalty_kernel(SampleState s) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x, u = r / s.B, lane = threadIdx.x;
   if (s.utt_done[u]) return;
   const int* h = s.hist + (int64_t)r * s.Tcap;
@@ -56,6 +58,8 @@ __device__ __forceinline__ ArgMax warp_argmax(ArgMax a) {
 
 // ---- greedy ----------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) greedy_kernel(SampleState s) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x, u = r;  // B == 1
   if (s.utt_done[u]) return;
   const float* lg = s.logits + (int64_t)r * s.V;
@@ -118,6 +122,8 @@ __device__ __forceinline__ void top_insert(float* v, int* ix, float nv, int ni) 
 }
 
 __global__ void __launch_bounds__(1024) topk_kernel(SampleState s) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x, u = r / s.B;
   if (s.utt_done[u]) return;
   const int n = s.len[r];
@@ -227,6 +233,8 @@ __global__ void __launch_bounds__(1024) topk_kernel(SampleState s) {
 constexpr int MAXB = 16;
 
 __global__ void __launch_bounds__(128) beam_update_kernel(SampleState s) {
+  pdl_trigger();
+  pdl_wait();
   const int u = blockIdx.x;
   if (s.utt_done[u]) return;
   const int B = s.B;
@@ -340,11 +348,15 @@ __global__ void __launch_bounds__(128) beam_update_kernel(SampleState s) {
 }
 
 __global__ void pos_inc_kernel(int* pos, int* step) {
+  pdl_trigger();
+  pdl_wait();
   *pos += 1;
   if (step) *step += 1;
 }
 
 __global__ void forced_kernel(SampleState s) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= s.R) return;
   const int tok = s.forced[(int64_t)(*s.step) * s.R + r];
@@ -355,6 +367,8 @@ __global__ void forced_kernel(SampleState s) {
 }
 
 __global__ void reset_kernel(SampleState s, const int* __restrict__ prompt) {
+  pdl_trigger();
+  pdl_wait();
   const int r = blockIdx.x;
   int* h = s.hist + (int64_t)r * s.Tcap;
   for (int i = threadIdx.x; i < s.P; i += blockDim.x) h[i] = prompt[i];
@@ -379,37 +393,28 @@ __global__ void reset_kernel(SampleState s, const int* __restrict__ prompt) {
 }  // namespace
 
 int launch_sample_step(const SampleState& s, cudaStream_t st) {
-  penalty_kernel<<<s.R, 32, 0, st>>>(s);
-  WG_CHECK(launch_status("penalty"));
+  WG_CHECK(launch_check(launch_k(penalty_kernel, dim3(s.R), dim3(32), 0, st, s), "penalty"));
   if (s.B <= 1) {
-    greedy_kernel<<<s.R, 1024, 0, st>>>(s);
-    WG_CHECK(launch_status("greedy"));
+    WG_CHECK(launch_check(launch_k(greedy_kernel, dim3(s.R), dim3(1024), 0, st, s), "greedy"));
   } else {
-    topk_kernel<<<s.R, 1024, 0, st>>>(s);
-    WG_CHECK(launch_status("topk"));
+    WG_CHECK(launch_check(launch_k(topk_kernel, dim3(s.R), dim3(1024), 0, st, s), "topk"));
     size_t dyn = (size_t)s.B * (s.Tcap + s.Tmax) * sizeof(int);
-    beam_update_kernel<<<s.U, 128, dyn, st>>>(s);
-    WG_CHECK(launch_status("beam_update"));
+    WG_CHECK(launch_check(launch_k(beam_update_kernel, dim3(s.U), dim3(128), dyn, st, s), "beam_update"));
   }
-  pos_inc_kernel<<<1, 1, 0, st>>>(s.pos, s.step);
-  return launch_status("pos_inc");
+  return launch_check(launch_k(pos_inc_kernel, dim3(1), dim3(1), 0, st, s.pos, s.step), "pos_inc");
 }
 
 int launch_forced_step(const SampleState& s, cudaStream_t st) {
-  forced_kernel<<<(s.R + 127) / 128, 128, 0, st>>>(s);
-  WG_CHECK(launch_status("forced"));
-  pos_inc_kernel<<<1, 1, 0, st>>>(s.pos, s.step);
-  return launch_status("pos_inc");
+  WG_CHECK(launch_check(launch_k(forced_kernel, dim3((s.R + 127) / 128), dim3(128), 0, st, s), "forced"));
+  return launch_check(launch_k(pos_inc_kernel, dim3(1), dim3(1), 0, st, s.pos, s.step), "pos_inc");
 }
 
 int launch_pos_inc(const SampleState& s, cudaStream_t st) {
-  pos_inc_kernel<<<1, 1, 0, st>>>(s.pos, nullptr);
-  return launch_status("pos_inc");
+  return launch_check(launch_k(pos_inc_kernel, dim3(1), dim3(1), 0, st, s.pos, (int*)nullptr), "pos_inc");
 }
 
 int launch_sample_reset(const SampleState& s, const int* prompt_dev, cudaStream_t st) {
-  reset_kernel<<<s.R, 128, 0, st>>>(s, prompt_dev);
-  return launch_status("sample_reset");
+  return launch_check(launch_k(reset_kernel, dim3(s.R), dim3(128), 0, st, s, prompt_dev), "sample_reset");
 }
 
 }  // namespace wg
