@@ -93,9 +93,13 @@ inline int launch_check(cudaError_t e, const char* what) {
 // Quantised matrices [rows, cols] (cols % 64 == 0) are repacked at upload into
 // the "tile128" layout consumed by the tensor-core GEMV/GEMM: rows are grouped
 // in tiles of 16, columns in quant blocks of 32; for every (tile, block) each
-// of the 32 lanes of a warp owns a contiguous payload that is exactly its
-// A-fragment of two mma.m16n8k16 steps (rows g and g+8, k = 2t,2t+1,2t+8,2t+9
-// and +16; g = lane/4, t = lane%4). The (tile, block) "slots" are ordered so
+// of the 32 lanes of a warp owns a contiguous payload: for each of the two
+// 16-wide K steps, rows g and g+8 at k = 4t..4t+3 (g = lane/4, t = lane%4),
+// i.e. the A fragment of mma.m16n8k16 with K permuted inside each 16 (the
+// mma kernels permute the B fragment the same way) and exactly the register
+// layout of a tcgen05.st.16x256b store of the dequantised tile into tensor
+// memory (registers: row g k 4t..4t+1, row g k 4t+2..4t+3, row g+8 ...).
+// The (tile, block) "slots" are ordered so
 // that the 8 tiles x 2 blocks of one 128-row x 64-column group are one
 // contiguous run (one bulk copy per tensor-core pipeline stage):
 //   slot(tile, kb) = (((tile/8) * (kb_count/2) + kb/2) * 8 + tile%8) * 2 + kb%2

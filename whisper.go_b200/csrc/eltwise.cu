@@ -11,7 +11,7 @@ __device__ __forceinline__ float dmat_elem(const DMat& m, int r, int k) {
   if (m.qtype == WG_QTYPE_F16) return __half2float(reinterpret_cast<const __half*>(m.qs)[(int64_t)r * m.cols + k]);
   int tile = r >> 4, gg = r & 15, g = gg & 7, hi = gg >> 3;
   int kb = k >> 5, kk = k & 31, s = kk >> 4, kr = kk & 15;
-  int t = (kr & 7) >> 1, e = kr & 1, reg = ((kr >> 3) << 1) | hi;
+  int t = kr >> 2, e = kr & 1, reg = (((kr >> 1) & 1) << 1) | hi;
   int lane = g * 4 + t;
   int64_t slot = slot_of(m, tile, kb);
   __half2 dd = m.dsc[slot * 8 + g];

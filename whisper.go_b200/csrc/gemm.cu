@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(SMALL_WK * 32)
   extern __shared__ __align__(16) unsigned char smem[];
   constexpr int RC = NB * 8;
   const int K = W.cols, KB = W.kblocks;
-  const int xs = K + 8;  // padded row stride in halves: conflict-free B-fragment loads
+  const int xs = K + 16;  // padded row stride in halves: conflict-free 8-byte B-fragment loads
   __half* xsm = reinterpret_cast<__half*>(smem);
   const int tile = blockIdx.x;
   const int r0 = blockIdx.y * RC;
@@ -279,13 +279,13 @@ __global__ void __launch_bounds__(SMALL_WK * 32)
         for (int s = 0; s < 2; s++) {
           uint32_t a[4];
           dequant_step<QT>(p[i], s, a);
-          const int k0 = kb * 32 + s * 16 + 2 * t;
+          // the payload's K order within 16 (lane t: k = 4t..4t+3) is the
+          // order of the B fragment: one 8-byte load
+          const int k0 = kb * 32 + s * 16 + 4 * t;
 #pragma unroll
           for (int nb = 0; nb < NB; nb++) {
-            const __half* xr = xsm + (nb * 8 + g) * xs + k0;
-            uint32_t b0 = *reinterpret_cast<const uint32_t*>(xr);
-            uint32_t b1 = *reinterpret_cast<const uint32_t*>(xr + 8);
-            mma16816(acc[nb], a, b0, b1);
+            const uint2 bb = *reinterpret_cast<const uint2*>(xsm + (nb * 8 + g) * xs + k0);
+            mma16816(acc[nb], a, bb.x, bb.y);
           }
         }
       }
@@ -307,7 +307,7 @@ __global__ void __launch_bounds__(SMALL_WK * 32)
 }
 
 // ---- large-R kernel ------------------------------------------------------------------
-constexpr int LG_RC = 64, LG_NB = 8, LG_STAGES = 4, LG_XS = 40;
+constexpr int LG_RC = 64, LG_NB = 8, LG_STAGES = 4, LG_XS = 48;  // row stride: conflict-free 8-byte loads
 
 template <uint32_t QT>
 __global__ void __launch_bounds__(128) gemm_large_kernel(DMat W, const __half* __restrict__ X, int ldx, Epi e) {
@@ -355,10 +355,8 @@ __global__ void __launch_bounds__(128) gemm_large_kernel(DMat W, const __half* _
       dequant_step<QT>(pcur, s, a);
 #pragma unroll
       for (int nb = 0; nb < LG_NB; nb++) {
-        const __half* xr = xb + (nb * 8 + g) * LG_XS + s * 16 + 2 * t;
-        uint32_t b0 = *reinterpret_cast<const uint32_t*>(xr);
-        uint32_t b1 = *reinterpret_cast<const uint32_t*>(xr + 8);
-        mma16816(acc[nb], a, b0, b1);
+        const uint2 bb = *reinterpret_cast<const uint2*>(xb + (nb * 8 + g) * LG_XS + s * 16 + 4 * t);
+        mma16816(acc[nb], a, bb.x, bb.y);
       }
     }
     pcur = pnext;
@@ -400,7 +398,7 @@ int configure_small_t() {
 template <uint32_t QT, int NB>
 int launch_small_t(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st) {
   constexpr int RC = NB * 8;
-  size_t smem = (size_t)RC * (W.cols + 8) * 2 + (size_t)SMALL_WK * NB * 4 * 32 * 4;
+  size_t smem = (size_t)RC * (W.cols + 16) * 2 + (size_t)SMALL_WK * NB * 4 * 32 * 4;
   if (smem > 227 * 1024) {
     set_error("gemv: K=%d too large for the small-R kernel", W.cols);
     return WG_ERR_UNSUPPORTED;

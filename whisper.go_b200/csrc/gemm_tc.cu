@@ -10,15 +10,16 @@
 // M = 128 weight rows per CTA and N = NR activation rows (<= 256).
 //
 // Per 64-wide K stage (ring of `stages` buffers, mbarrier handshakes):
-//   warp 10 (one thread): cp.async.bulk of the raw quant payloads of the
+//   warp 18 (one thread): cp.async.bulk of the raw quant payloads of the
 //     CTA's 128 x 64 weight group (16 contiguous tile128 slots: one copy per
 //     plane) -> RAW[s], a ring of TC_DQ_NS stages
-//   warp 9 (one thread): TMA 2-D tile load of X[NR, 64] (f16, 128B swizzle)
-//     -> B[s]
-//   warps 0-7: warp w dequantises row tile w of RAW[s] -> A[s] (f16 = d*q
-//     rounded once, stored with stmatrix in the 128B-swizzled K-major
-//     canonical layout TMA writes for B)
-//   warp 8 (one thread): 4 x tcgen05.mma.kind::f16 (K=16) into TMEM, then
+//   warp 17 (one thread): TMA 2-D tile load of X[NR, 64] (f16, 128B swizzle)
+//     -> B[s] in shared memory
+//   warps 0-15: two groups of 8 on alternating stages; each warp dequantises
+//     one row tile of RAW[s] (f16 = d*q rounded once) and stores it into
+//     the stage's A tile in tensor memory (tcgen05.st.16x256b)
+//   warp 16 (one thread): 4 x tcgen05.mma.kind::f16 (K=16, A from tensor
+//     memory, B from shared memory) into the TMEM accumulator, then
 //     tcgen05.commit frees the stage
 // K may be split over a thread-block cluster of ks CTAs (grid z); the
 // epilogue then reduces the partial tiles through distributed shared memory
@@ -59,10 +60,6 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
   return d;
 }
 
-// Byte offset of element (row, k) of a [rows][64] f16 tile in the 128B-swizzled layout.
-__device__ __forceinline__ uint32_t sw128_off(int row, int k) {
-  return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
-}
 
 __device__ __forceinline__ uint32_t h2u(__half2 h) {
   uint32_t u;
@@ -76,29 +73,31 @@ __device__ __forceinline__ __half2 u2h(uint32_t u) {
 }
 
 // ---- epilogue (shared with gemm.cu's semantics) --------------------------------
-// Shared memory: S stages of {A (dequantised weights), B (activation
-// tile)}, as many as fit in 220 KB next to the RAW ring (TC_DQ_NS stages of
-// quant payloads), then the mbarriers.
-constexpr int TC_S_MAX = 6;
+// Shared memory: S stages of B (activation tiles), as many as fit in 220 KB
+// next to the RAW ring (TC_DQ_NS stages of quant payloads), then the
+// mbarriers. The dequantised A tiles live in tensor memory: stage s at
+// columns TC_A_COL + 32*s (128 lanes x 64 f16), the accumulator at columns
+// 0..NR-1 (NR <= 256).
+constexpr int TC_S_MAX = 8;
+constexpr uint32_t TC_A_COL = 256;
+constexpr uint32_t TC_TMEM_COLS = 512;
 struct TcLayout {
   int stages;                    // A/B ring depth
-  uint32_t a_bytes, b_bytes;
+  uint32_t b_bytes;
   uint32_t raw_bytes;            // one RAW stage: 16 slots x {32 x pb | d | m | hb}
-  uint32_t a0, b0, raw0, bar0, total;
+  uint32_t b0, raw0, bar0, total;
 };
 
 __host__ __device__ inline TcLayout tc_layout(uint32_t qt, int NR) {
   TcLayout L{};
-  L.a_bytes = TC_BM * TC_BK * 2;  // 16 KB
   L.b_bytes = (uint32_t)NR * TC_BK * 2;
   // d at 16*32*pb, m at +512, hb at +1024 (the m gap is kept when only hb is present)
   L.raw_bytes = 16 * 32 * qtype_payload_bytes(qt) + 512 + ((qtype_has_min(qt) || qtype_has_hbits(qt)) ? 512 : 0) +
                 (qtype_has_hbits(qt) ? 1024 : 0);
   const uint32_t raw = TC_DQ_NS * L.raw_bytes;
-  L.stages = (int)((220u * 1024u - raw) / (L.a_bytes + L.b_bytes));
+  L.stages = (int)((220u * 1024u - raw) / L.b_bytes);
   if (L.stages > TC_S_MAX) L.stages = TC_S_MAX;
-  L.a0 = 0;
-  L.b0 = L.a0 + L.stages * L.a_bytes;
+  L.b0 = 0;
   L.raw0 = L.b0 + L.stages * L.b_bytes;
   L.bar0 = L.raw0 + raw;
   L.total = L.bar0 + 8 * (2 * TC_S_MAX + 2 * TC_DQ_NS + 1) + 16 + 1024;  // barriers, tmem slot, slack
@@ -260,8 +259,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  uint32_t ncols = 32;
-  while (ncols < (uint32_t)NR) ncols <<= 1;
+  const uint32_t ncols = TC_TMEM_COLS;
   if (warp == TC_MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(ncols)
@@ -318,15 +316,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int s = kl % S;
         if (!mbar_wait(FULL(s), (uint32_t)(kl / S) & 1u, abort_flag, (kl << 8) | 3, &g_tc_error)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint64_t ad = sw128_desc(base + L.a0 + s * L.a_bytes);
+        const uint32_t at = tmem + TC_A_COL + 32u * (uint32_t)s;  // A in tensor memory
         const uint64_t bd = sw128_desc(base + L.b0 + s * L.b_bytes);
 #pragma unroll
         for (int kk = 0; kk < 4; kk++) {
           const uint32_t acc = (kl > 0 || kk > 0) ? 1u : 0u;
           asm volatile(
               "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-              " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
-              "l"(ad + (uint64_t)(kk * 2)), "l"(bd + (uint64_t)(kk * 2)), "r"(idesc), "r"(acc)
+              " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem),
+              "r"(at + (uint32_t)(kk * 8)), "l"(bd + (uint64_t)(kk * 2)), "r"(idesc), "r"(acc)
               : "memory");
         }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(EMPTY(s))
@@ -338,23 +336,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else {
     // ---------------- dequantisers ----------------
     // group grp = warp / 8 takes the stages kl = grp (mod 2), so the two
-    // groups' wait / dequantise / fence chains overlap; warp w of a group
-    // owns row tile w (rows 16w..16w+15) of the stage
-    const int g = lane >> 2, grp = warp >> 3, tile = warp & 7;
+    // groups' wait / dequantise / store chains overlap. Warp w may only
+    // address tensor-memory lanes 32(w%4)..32(w%4)+31, so it owns row tile
+    // 2(w%4) + (w/4)%2 (rows = TMEM lanes 16*tile..16*tile+15)
+    const int g = lane >> 2, grp = warp >> 3, tile = 2 * (warp & 3) + ((warp >> 2) & 1);
+    const uint32_t tlane = (uint32_t)(16 * tile) << 16;
     // this warp's two slots (blocks 0/1 of its tile) inside a raw stage
     const uint32_t d_off = 16 * 32 * pb, m_off = d_off + 512, hb_off = m_off + 512;
     const unsigned char* rq = sm + L.raw0 + (2 * tile) * 32 * pb;
     const unsigned char* rd = sm + L.raw0 + d_off + (2 * tile) * 32;
     const unsigned char* rm = sm + L.raw0 + m_off + (2 * tile) * 32;
     const unsigned char* rh = sm + L.raw0 + hb_off + (2 * tile) * 64;
-    uint32_t soff[2][2];
-#pragma unroll
-    for (int blk = 0; blk < 2; blk++)
-#pragma unroll
-      for (int st = 0; st < 2; st++) {
-        const int mtx = lane >> 3;
-        soff[blk][st] = sw128_off(tile * 16 + (mtx & 1) * 8 + (lane & 7), blk * 32 + st * 16 + (mtx >> 1) * 8);
-      }
     for (int kl = grp; kl < nk; kl += 2) {
       const int s = kl % S;
       const uint32_t ph = (uint32_t)(kl / S) & 1u;
@@ -364,7 +356,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       const uint32_t ro = rs * L.raw_bytes;
-      const uint32_t abase = base + L.a0 + s * L.a_bytes;
+      uint32_t tr[16];  // the stage's 16 rows x 64 k in tcgen05.st.16x256b order
 #pragma unroll
       for (int blk = 0; blk < 2; blk++) {
         const __half2 dd = reinterpret_cast<const __half2*>(rd + ro)[blk * 8 + g];
@@ -410,13 +402,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               a[r] = h2u(v);
             }
           }
-          asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(abase +
-                                                                                                 soff[blk][st]),
-                       "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3])
-                       : "memory");
+          // a: (row g, k 4t..4t+1), (row g+8, same k), (row g, k 4t+2..4t+3), (row g+8, ...);
+          // the store wants row g's two 32-bit columns, then row g+8's
+          const int o = (blk * 2 + st) * 4;
+          tr[o] = a[0];
+          tr[o + 1] = a[2];
+          tr[o + 2] = a[1];
+          tr[o + 3] = a[3];
         }
       }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile(
+          "tcgen05.st.sync.aligned.16x256b.x4.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::
+              "r"(tmem + tlane + TC_A_COL + 32u * (uint32_t)s),
+          "r"(tr[0]), "r"(tr[1]), "r"(tr[2]), "r"(tr[3]), "r"(tr[4]), "r"(tr[5]), "r"(tr[6]), "r"(tr[7]), "r"(tr[8]),
+          "r"(tr[9]), "r"(tr[10]), "r"(tr[11]), "r"(tr[12]), "r"(tr[13]), "r"(tr[14]), "r"(tr[15])
+          : "memory");
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(RAW_EMPTY(rs));

@@ -55,7 +55,7 @@ __global__ void repack_tile16_kernel(uint32_t qtype, const uint8_t* __restrict__
     for (int j = 0; j < 16; j++) {
       int s = j >> 3, reg = (j & 7) >> 1, e = j & 1;
       const uint8_t* b = (reg & 1) ? b1 : b0;
-      int k = 16 * s + 2 * t + 8 * (reg >> 1) + e;
+      int k = 16 * s + 4 * t + 2 * (reg >> 1) + e;
       pay[j] = b ? b[off.qs + k] : 0;
     }
     uint4 v;
@@ -71,7 +71,7 @@ __global__ void repack_tile16_kernel(uint32_t qtype, const uint8_t* __restrict__
 #pragma unroll
       for (int p = 0; p < 4; p++) {
         const uint8_t* b = (p & 1) ? b1 : b0;
-        int k0 = 16 * s + 2 * t + 8 * (p >> 1);
+        int k0 = 16 * s + 4 * t + 2 * (p >> 1);
         uint32_t byte = b ? b[off.qs + k0 / 2] : 0x00;
         w[s] |= (byte & 0xF) << (4 * p);
         w[s] |= (byte >> 4) << (16 + 4 * p);
@@ -102,7 +102,7 @@ __global__ void dequant_tile16_kernel(DMat m, int64_t n_valid, float* __restrict
   int r = (int)(i / m.cols), k = (int)(i % m.cols);
   int tile = r >> 4, gg = r & 15, g = gg & 7, hi = gg >> 3;
   int kb = k >> 5, kk = k & 31, s = kk >> 4, kr = kk & 15;
-  int t = (kr & 7) >> 1, e = kr & 1, reg = ((kr >> 3) << 1) | hi;
+  int t = kr >> 2, e = kr & 1, reg = (((kr >> 1) & 1) << 1) | hi;
   int lane = g * 4 + t;
   int64_t slot = slot_of(m, tile, kb);
   __half2 dd = m.dsc[slot * 8 + g];
