@@ -146,3 +146,24 @@ def test_cancel_during_decode(tiny):
         for _ in range(1000):
             dec.decode(m.encoder_output(0), wgdec.DecoderParams(prompt=PROMPT, max_tokens=200), ctx)
     assert wgdec.is_canceled(ei.value)
+
+
+@pytest.mark.parametrize("qtype", ["Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q8_0"])
+def test_teacher_forced_tensor_core_path(qtype):
+    """20 utterances (R = 20 > 16): every GEMM of the step, the cross K/V
+    precompute and the logits run on the tcgen05 kernel (dequantised tiles
+    in tensor memory), with all epilogue modes (QKV scatter, residual add,
+    GELU, cross K/V scatter), for each quantisation type."""
+    m = wgdec.SyntheticModel(51864, 256, 4, 2, 448, qtype, seed=23)
+    dec = wgdec.WhisperDecoder(m)
+    try:
+        U, T = 20, 64
+        encs = [m.encoder_output(u, T) for u in range(U)]
+        forced = np.random.default_rng(5).integers(0, 50257, size=(U, 3))
+        gpu = dec.teacher_forced_logits(encs, PROMPT, forced, wgdec.MODE_CORRECT)
+        for u in range(U):
+            ref = oracle.teacher_forced(m, encs[u], PROMPT, forced[u], wgdec.MODE_CORRECT, m.n_vocab)
+            assert_logits_close(gpu[:, u, :], ref)
+    finally:
+        dec.close()
+        m.close()

@@ -1,6 +1,7 @@
 // sample.cu — on-device token selection of the decoder token loop.
 //
-//  penalty_kernel      applyRepetitionPenalty (internal/model/decoder.go:1140-1167)
+//  penalty_row         applyRepetitionPenalty (internal/model/decoder.go:1140-1167),
+//                      applied by greedy_kernel / topk_kernel to their row
 //  greedy_kernel       sampleGreedyWithScratch (:996-1059) + the greedy loop's
 //                      append / EOT / repeat-streak stops (:467-484)
 //  topk_kernel         topKTokensWithScratch (:1068-1136), k = 5
@@ -14,28 +15,33 @@ namespace wg {
 namespace {
 
 // ---- repetition penalty: logit[id] -= 2.0 * count(id in last 128 tokens) ----
-__global__ void penalty_kernel(SampleState s) {
-  pdl_trigger();
-  pdl_wait();
-  const int r = blockIdx.x, u = r / s.B, lane = threadIdx.x;
-  if (s.utt_done[u]) return;
-  const int* h = s.hist + (int64_t)r * s.Tcap;
+// One row, by the whole CTA, at the start of the row's sampling kernel: the
+// history window is staged in shared memory; the thread holding the first
+// occurrence of an id applies its count (decoder.go:1140-1167), then EOT is
+// masked when suppress_eot is set. Ends with a CTA barrier, so the row's
+// logits are final for every thread afterwards.
+constexpr int PEN_WIN = 128;
+__device__ void penalty_row(const SampleState& s, int r) {
+  __shared__ int hs[PEN_WIN];
   const int n = s.len[r];
-  const int start = n > 128 ? n - 128 : 0;
+  const int start = n > PEN_WIN ? n - PEN_WIN : 0, cnt = n - start;
+  const int* h = s.hist + (int64_t)r * s.Tcap;
+  for (int i = threadIdx.x; i < cnt; i += blockDim.x) hs[i] = h[start + i];
+  __syncthreads();
   float* lg = s.logits + (int64_t)r * s.V;
-  for (int i = start + lane; i < n; i += 32) {
-    int id = h[i];
+  for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
+    const int id = hs[i];
     if (id < 0 || id >= s.V) continue;
     bool first = true;
-    for (int j = start; j < i; j++)
-      if (h[j] == id) { first = false; break; }
+    for (int j = 0; j < i && first; j++) first = hs[j] != id;
     if (!first) continue;
-    int cnt = 0;
-    for (int j = i; j < n; j++) cnt += h[j] == id;
-    lg[id] = __fsub_rn(lg[id], __fmul_rn(2.0f, (float)cnt));
+    int c = 0;
+    for (int j = i; j < cnt; j++) c += hs[j] == id;
+    lg[id] = __fsub_rn(lg[id], __fmul_rn(2.0f, (float)c));
   }
-  __syncwarp();
-  if (lane == 0 && s.suppress_eot && s.eot >= 0 && s.eot < s.V) lg[s.eot] = -INFINITY;
+  __syncthreads();
+  if (threadIdx.x == 0 && s.suppress_eot && s.eot >= 0 && s.eot < s.V) lg[s.eot] = -INFINITY;
+  __syncthreads();
 }
 
 struct ArgMax {
@@ -62,6 +68,7 @@ __global__ void __launch_bounds__(1024) greedy_kernel(SampleState s) {
   pdl_wait();
   const int r = blockIdx.x, u = r;  // B == 1
   if (s.utt_done[u]) return;
+  penalty_row(s, r);
   const float* lg = s.logits + (int64_t)r * s.V;
   ArgMax all{-INFINITY, -1}, excl{-INFINITY, -1};
   for (int i = threadIdx.x; i < s.V; i += blockDim.x) {
@@ -121,7 +128,8 @@ __device__ __forceinline__ void top_insert(float* v, int* ix, float nv, int ni) 
   ix[j] = ni;
 }
 
-__global__ void __launch_bounds__(1024) topk_kernel(SampleState s) {
+constexpr int TOPK_THREADS = 512;  // one wave of rows (four CTAs per SM)
+__global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(SampleState s) {
   pdl_trigger();
   pdl_wait();
   const int r = blockIdx.x, u = r / s.B;
@@ -129,6 +137,7 @@ __global__ void __launch_bounds__(1024) topk_kernel(SampleState s) {
   const int n = s.len[r];
   const int* h = s.hist + (int64_t)r * s.Tcap;
   if (n > 0 && h[n - 1] == s.eot) return;  // finished hypothesis: carried forward unchanged
+  penalty_row(s, r);
   const float* lg = s.logits + (int64_t)r * s.V;
   float tv[TOPK];
   int ti[TOPK];
@@ -163,10 +172,11 @@ __global__ void __launch_bounds__(1024) topk_kernel(SampleState s) {
   }
   __syncthreads();
   mx = smax;
-  // expSum = sum float32(exp(float64(s - max)))  (decoder.go:1121-1124)
+  // expSum = sum float32(exp(float64(s - max)))  (decoder.go:1121-1124); the
+  // terms in float32 (expf, within 2 ulp of the rounded float64 value: the
+  // reference's sequential float32 sum is reordered here anyway)
   float es = 0.f;
-  for (int i = threadIdx.x; i < s.V; i += blockDim.x)
-    es += (float)exp((double)__fsub_rn(__fmul_rn(lg[i], s.inv_temp), mx));
+  for (int i = threadIdx.x; i < s.V; i += blockDim.x) es += expf(__fsub_rn(__fmul_rn(lg[i], s.inv_temp), mx));
   es = warp_sum(es);
   __syncthreads();
   if (lane == 0) wsum[warp] = es;
@@ -393,11 +403,10 @@ __global__ void reset_kernel(SampleState s, const int* __restrict__ prompt) {
 }  // namespace
 
 int launch_sample_step(const SampleState& s, cudaStream_t st) {
-  WG_CHECK(launch_check(launch_k(penalty_kernel, dim3(s.R), dim3(32), 0, st, s), "penalty"));
   if (s.B <= 1) {
     WG_CHECK(launch_check(launch_k(greedy_kernel, dim3(s.R), dim3(1024), 0, st, s), "greedy"));
   } else {
-    WG_CHECK(launch_check(launch_k(topk_kernel, dim3(s.R), dim3(1024), 0, st, s), "topk"));
+    WG_CHECK(launch_check(launch_k(topk_kernel, dim3(s.R), dim3(TOPK_THREADS), 0, st, s), "topk"));
     size_t dyn = (size_t)s.B * (s.Tcap + s.Tmax) * sizeof(int);
     WG_CHECK(launch_check(launch_k(beam_update_kernel, dim3(s.U), dim3(128), dyn, st, s), "beam_update"));
   }
