@@ -96,6 +96,7 @@ struct DevJob {
   int* forced_dev = nullptr;
   int* ints = nullptr;
   float* floats = nullptr;
+  float* split_ws = nullptr;  // tcgen05 split-K partial tiles (TC_SPLIT_WS_FLOATS)
   SampleState ss{};
   int* host_done = nullptr;  // pinned
   cudaGraphExec_t graph = nullptr;
@@ -103,6 +104,14 @@ struct DevJob {
   bool started = false;
   cudaEvent_t ev[2] = {nullptr, nullptr};
 };
+
+// An epilogue descriptor carrying the job's split-K workspace.
+inline Epi job_epi(const DevJob& j) {
+  Epi e;
+  e.split_ws = j.split_ws;
+  e.split_ws_floats = TC_SPLIT_WS_FLOATS;
+  return e;
+}
 
 }  // namespace
 }  // namespace wg
@@ -268,7 +277,7 @@ int forward_step(wg_model* m, DevJob& j, const int* tokens, bool want_logits, in
     __half* kv = j.selfkv + l * layer_kv;
     // self-attention (decoder.go:836-908)
     WG_CHECK(launch_layernorm(j.x, ly.sln_w, ly.sln_b, R, d, j.xln16, nullptr, st));
-    Epi e;
+    Epi e = job_epi(j);
     e.mode = EPI_QKV; e.out = j.q; e.ldo = d; e.d = d; e.H = H; e.hd = hd; e.T = j.Tmax; e.pos = j.ss.pos;
     e.kv = kv; e.bias_q = ly.q_b; e.bias_v = ly.v_b; e.N = 3 * d;
     WG_CHECK(launch_matmul(ly.qkv, j.xln16, j.ldd, R, e, st));
@@ -277,28 +286,28 @@ int forward_step(wg_model* m, DevJob& j, const int* tokens, bool want_logits, in
     sa.R = R; sa.H = H; sa.hd = hd; sa.Tmax = j.Tmax; sa.ref_compat = ref; sa.zero_unless_pos0 = ref && j.B > 1;
     sa.out16 = j.attn16;
     WG_CHECK(launch_self_attn(sa, st));
-    e = Epi(); e.mode = EPI_RESID; e.out = j.x; e.ldo = d; e.bias = ly.so_b; e.N = d;
+    e = job_epi(j); e.mode = EPI_RESID; e.out = j.x; e.ldo = d; e.bias = ly.so_b; e.N = d;
     WG_CHECK(launch_matmul(ly.so, j.attn16, j.ldd, R, e, st));
     // cross-attention (decoder.go:911-971)
     WG_CHECK(launch_layernorm(j.x, ly.cln_w, ly.cln_b, R, d, j.xln16, nullptr, st));
-    e = Epi(); e.mode = EPI_F32; e.out = j.q; e.ldo = d; e.bias = ly.cq_b; e.N = d;
+    e = job_epi(j); e.mode = EPI_F32; e.out = j.q; e.ldo = d; e.bias = ly.cq_b; e.N = d;
     WG_CHECK(launch_matmul(ly.cq, j.xln16, j.ldd, R, e, st));
     CrossAttnArgs ca{};
     ca.q = j.q; ca.kv = j.cross + l * layer_cross; ca.U = j.U; ca.B = j.B; ca.H = H; ca.hd = hd; ca.T = j.T;
     ca.out16 = j.attn16;
     WG_CHECK(launch_cross_attn(ca, st));
-    e = Epi(); e.mode = EPI_RESID; e.out = j.x; e.ldo = d; e.bias = ly.co_b; e.N = d;
+    e = job_epi(j); e.mode = EPI_RESID; e.out = j.x; e.ldo = d; e.bias = ly.co_b; e.N = d;
     WG_CHECK(launch_matmul(ly.co, j.attn16, j.ldd, R, e, st));
     // MLP (decoder.go:974-993)
     WG_CHECK(launch_layernorm(j.x, ly.mln_w, ly.mln_b, R, d, j.xln16, nullptr, st));
-    e = Epi(); e.mode = EPI_GELU_F16; e.out16 = j.h16; e.ldo = j.ld4; e.bias = ly.m0_b; e.N = 4 * d;
+    e = job_epi(j); e.mode = EPI_GELU_F16; e.out16 = j.h16; e.ldo = j.ld4; e.bias = ly.m0_b; e.N = 4 * d;
     WG_CHECK(launch_matmul(ly.m0, j.xln16, j.ldd, R, e, st));
-    e = Epi(); e.mode = EPI_RESID; e.out = j.x; e.ldo = d; e.bias = ly.m2_b; e.N = d;
+    e = job_epi(j); e.mode = EPI_RESID; e.out = j.x; e.ldo = d; e.bias = ly.m2_b; e.N = d;
     WG_CHECK(launch_matmul(ly.m2, j.h16, j.ld4, R, e, st));
   }
   if (!want_logits) return WG_OK;
   WG_CHECK(launch_layernorm(j.x, dm.ln_w, dm.ln_b, R, d, j.xln16, nullptr, st));  // decoder.go:818
-  Epi e;
+  Epi e = job_epi(j);
   e.mode = EPI_F32; e.out = j.logits; e.ldo = m->V; e.N = m->V;
   return launch_matmul(dm.tok, j.xln16, j.ldd, R, e, st);  // decoder.go:823 (tied embedding)
 }
@@ -317,6 +326,7 @@ void free_devjob(DevJob* j) {
   cudaFree(j->enc32); cudaFree(j->enc16); cudaFree(j->cross); cudaFree(j->selfkv);
   cudaFree(j->x); cudaFree(j->q); cudaFree(j->logits); cudaFree(j->xln16); cudaFree(j->attn16); cudaFree(j->h16);
   cudaFree(j->ptok); cudaFree(j->prompt_dev); cudaFree(j->forced_dev); cudaFree(j->ints); cudaFree(j->floats);
+  cudaFree(j->split_ws);
   if (j->host_done) cudaFreeHost(j->host_done);
   for (auto& e : j->ev)
     if (e) cudaEventDestroy(e);
@@ -375,7 +385,9 @@ int build_devjob(wg_job* J, DevModel* dm, const std::vector<int>& utt, DevJob** 
   // integer / float state
   const size_t n_ints = (size_t)R * j->Tcap * 2 + (size_t)R * j->Tmax * 2 + (size_t)R * 16 + (size_t)U * 2 + 8;
   const size_t n_floats = (size_t)R * 8;
-  if ((rc = dalloc(&j->ints, n_ints)) || (rc = dalloc(&j->floats, n_floats))) return fail(rc);
+  if ((rc = dalloc(&j->ints, n_ints)) || (rc = dalloc(&j->floats, n_floats)) ||
+      (rc = dalloc(&j->split_ws, (size_t)TC_SPLIT_WS_FLOATS)))
+    return fail(rc);
   int* ip = j->ints;
   auto take = [&](size_t n) {
     int* p = ip;
@@ -450,7 +462,7 @@ int start_devjob(wg_job* J, DevJob& j) {
       WG_CHECK(launch_f32_to_f16(j.enc32 + r * d, j.enc16 + r * j.ldd, d, j.st));
   }
   // K_c = E Wk^T, V_c = E Wv^T + vB for all layers at once (decoder.go:923-940)
-  Epi e;
+  Epi e = job_epi(j);
   e.mode = EPI_CROSS_KV; e.kv = j.cross; e.d = d; e.H = m->H; e.hd = m->hd; e.T = j.T; e.U = j.U;
   e.bias_v = j.dm->cross_vb; e.N = 2 * m->L * d;
   WG_CHECK(launch_matmul(j.dm->cross_kv, j.enc16, j.ldd, j.U * j.T, e, j.st));
@@ -956,8 +968,9 @@ int wg_matmul_test(uint32_t qtype, const void* raw, int rows, int cols, const fl
   DMat dm;
   int rc = upload_matrix(parts, 1, &dm, st);
   const int ld = round8(cols);
-  float *dx = nullptr, *dout = nullptr;
+  float *dx = nullptr, *dout = nullptr, *ws = nullptr;
   __half* dx16 = nullptr;
+  if (rc == WG_OK) rc = dalloc(&ws, (size_t)TC_SPLIT_WS_FLOATS);
   if (rc == WG_OK) rc = dalloc(&dx, (size_t)M * cols);
   if (rc == WG_OK) rc = dalloc(&dx16, (size_t)M * ld);
   if (rc == WG_OK) rc = dalloc(&dout, (size_t)M * rows);
@@ -969,6 +982,7 @@ int wg_matmul_test(uint32_t qtype, const void* raw, int rows, int cols, const fl
   if (rc == WG_OK) {
     Epi e;
     e.mode = EPI_F32; e.out = dout; e.ldo = rows; e.N = rows;
+    e.split_ws = ws; e.split_ws_floats = TC_SPLIT_WS_FLOATS;
     rc = launch_matmul(dm, dx16, ld, M, e, st, path);
   }
   if (rc == WG_OK && cudaMemcpyAsync(out, dout, (size_t)M * rows * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) {
@@ -979,7 +993,7 @@ int wg_matmul_test(uint32_t qtype, const void* raw, int rows, int cols, const fl
   if (rc == WG_OK) {
     rc = check_wait_flags();
   }
-  cudaFree(dx); cudaFree(dx16); cudaFree(dout);
+  cudaFree(dx); cudaFree(dx16); cudaFree(dout); cudaFree(ws);
   free_dmat(dm);
   cudaStreamDestroy(st);
   return rc;
@@ -1008,7 +1022,7 @@ int wg_job_time_kernel(wg_job* J, int kclass, int iters, double* ms, double* byt
         const DMat* mats[6] = {&ly.qkv, &ly.so, &ly.cq, &ly.co, &ly.m0, &ly.m2};
         for (int k = 0; k < 6; k++) {
           if (kclass != WG_KCLASS_GEMV && k != kclass - WG_KCLASS_MATMUL0) continue;
-          Epi e;
+          Epi e = job_epi(j);
           const __half* xin = k == 5 ? j.h16 : (k == 1 || k == 3 ? j.attn16 : j.xln16);
           int ldx = k == 5 ? j.ld4 : j.ldd;
           if (k == 4) { e.mode = EPI_GELU_F16; e.out16 = j.h16; e.ldo = j.ld4; e.bias = ly.m0_b; }
@@ -1042,7 +1056,7 @@ int wg_job_time_kernel(wg_job* J, int kclass, int iters, double* ms, double* byt
         }
       } else if (kclass == WG_KCLASS_PRECOMPUTE) {
         if (l > 0) break;
-        Epi e;
+        Epi e = job_epi(j);
         e.mode = EPI_CROSS_KV; e.kv = j.cross; e.d = d; e.H = H; e.hd = hd; e.T = j.T; e.U = j.U;
         e.bias_v = dm.cross_vb; e.N = 2 * L * d;
         WG_CHECK(launch_matmul(dm.cross_kv, j.enc16, j.ldd, j.U * j.T, e, j.st));
@@ -1052,7 +1066,7 @@ int wg_job_time_kernel(wg_job* J, int kclass, int iters, double* ms, double* byt
         }
       } else if (kclass == WG_KCLASS_LOGITS) {
         if (l > 0) break;
-        Epi e;
+        Epi e = job_epi(j);
         e.mode = EPI_F32; e.out = j.logits; e.ldo = m->V; e.N = m->V;
         WG_CHECK(launch_matmul(dm.tok, j.xln16, j.ldd, R, e, j.st));
         if (count) {

@@ -139,6 +139,18 @@ __device__ __forceinline__ TcEpiRow tc_epi_row(const Epi& e, int n) {
   return er;
 }
 
+// Bias of weight row n (model data only; no state written by the token loop).
+__device__ __forceinline__ float tc_epi_bias(const Epi& e, int n) {
+  if (n >= e.N) return 0.f;
+  if (e.mode == EPI_F32 || e.mode == EPI_RESID || e.mode == EPI_GELU_F16) return e.bias ? e.bias[n] : 0.f;
+  if (e.mode == EPI_QKV) {
+    const int seg = n / e.d, j = n - seg * e.d;
+    return seg == 0 ? e.bias_q[j] : (seg == 2 ? e.bias_v[j] : 0.f);
+  }
+  const int lk = n / e.d, j = n - lk * e.d;  // EPI_CROSS_KV
+  return (lk & 1) ? e.bias_v[(int64_t)(lk >> 1) * e.d + j] : 0.f;
+}
+
 // Stores acc of rows r0, r0+1, ..., r0+cnt-1 (v[i] for row r0+i) of weight row n.
 template <int CNT>
 __device__ __forceinline__ void tc_epi_store_run(const Epi& e, const TcEpiRow& er, bool qkv_q, int r0, int R,
@@ -246,14 +258,39 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint32_t DONE = bar + 8 * NBAR;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L.bar0 + 8 * (NBAR + 1));
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L.bar0 + 8 * (NBAR + 1) + 4);
+  constexpr int pb = QT == WG_QTYPE_Q8_0 ? 16 : 8;
+  constexpr bool has_m = QT == WG_QTYPE_Q4_1 || QT == WG_QTYPE_Q5_1;
+  constexpr bool has_h = QT == WG_QTYPE_Q5_0 || QT == WG_QTYPE_Q5_1;
+  // weight stage kl: bulk copies of its 16 contiguous slots into the RAW ring
+  // raw ring slot (per stage): qs [16][32][pb] | d [16][8] half2 | m [16][8] half2 | hb [16][32] u16
+  auto issue_weights = [&](int kl) {
+    constexpr uint32_t qs_b = 16 * 32 * pb;
+    constexpr uint32_t tx = qs_b + 512 + (has_m ? 512 : 0) + (has_h ? 1024 : 0);
+    const int s = kl % TC_DQ_NS;
+    const uint32_t dst = base + L.raw0 + s * L.raw_bytes;
+    const int64_t g0 = slot_of(W, tile0, 2 * kstage(kl));  // 16 contiguous slots: tile t, blocks 0/1
+    mbar_arrive_tx(RAW_FULL(s), tx);
+    bulk_g2s(dst, W.qs + g0 * 32 * pb, qs_b, RAW_FULL(s));
+    bulk_g2s(dst + qs_b, W.dsc + g0 * 8, 512, RAW_FULL(s));
+    if (has_m) bulk_g2s(dst + qs_b + 512, W.msc + g0 * 8, 512, RAW_FULL(s));
+    if (has_h) bulk_g2s(dst + qs_b + 1024, W.hb + g0 * 32, 1024, RAW_FULL(s));
+  };
+  // The weight loader initialises the RAW ring's barriers itself and issues
+  // the ring's first stages at once (their slots are free), so the weight
+  // stream overlaps the TMEM allocation and the block barrier below.
+  const int n_pre = min(nk, TC_DQ_NS);
+  if (warp == TC_WLOAD_WARP && lane == 0) {
+    for (int s = 0; s < TC_DQ_NS; s++) {
+      mbar_init(RAW_FULL(s), 1);
+      mbar_init(RAW_EMPTY(s), 8);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int kl = 0; kl < n_pre; kl++) issue_weights(kl);
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; s++) {
       mbar_init(FULL(s), 8 + 1);
       mbar_init(EMPTY(s), 1);
-    }
-    for (int s = 0; s < TC_DQ_NS; s++) {
-      mbar_init(RAW_FULL(s), 1);
-      mbar_init(RAW_EMPTY(s), 8);
     }
     mbar_init(DONE, 1);
     *abort_flag = 0;
@@ -270,27 +307,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
-  const int pb = QT == WG_QTYPE_Q8_0 ? 16 : 8;
-  const bool has_m = QT == WG_QTYPE_Q4_1 || QT == WG_QTYPE_Q5_1;
-  const bool has_h = QT == WG_QTYPE_Q5_0 || QT == WG_QTYPE_Q5_1;
 
   if (warp == TC_WLOAD_WARP) {
     if (lane == 0) {
-      // ---------------- weight loader: bulk copies of the stage's 16 contiguous slots ----------------
-      // raw ring slot (per stage): qs [16][32][pb] | d [16][8] half2 | m [16][8] half2 | hb [16][32] u16
-      const uint32_t qs_b = 16 * 32 * pb;
-      const uint32_t tx = qs_b + 512 + (has_m ? 512 : 0) + (has_h ? 1024 : 0);
-      for (int kl = 0; kl < nk; kl++) {
+      // ---------------- weight loader: the remaining stages ----------------
+      for (int kl = n_pre; kl < nk; kl++) {
         const int s = kl % TC_DQ_NS;
         const uint32_t ph = (uint32_t)(kl / TC_DQ_NS) & 1u;
         if (!mbar_wait(RAW_EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 1, &g_tc_error)) break;
-        const uint32_t dst = base + L.raw0 + s * L.raw_bytes;
-        const int64_t g0 = slot_of(W, tile0, 2 * kstage(kl));  // 16 contiguous slots: tile t, blocks 0/1
-        mbar_arrive_tx(RAW_FULL(s), tx);
-        bulk_g2s(dst, W.qs + g0 * 32 * pb, qs_b, RAW_FULL(s));
-        bulk_g2s(dst + qs_b, W.dsc + g0 * 8, 512, RAW_FULL(s));
-        if (has_m) bulk_g2s(dst + qs_b + 512, W.msc + g0 * 8, 512, RAW_FULL(s));
-        if (has_h) bulk_g2s(dst + qs_b + 1024, W.hb + g0 * 32, 1024, RAW_FULL(s));
+        issue_weights(kl);
       }
     }
   } else if (warp == TC_XLOAD_WARP) {
@@ -428,34 +453,44 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
 
   // ---------------- epilogue ----------------
-  // (1) warps 0-7 move the fp32 accumulator tile out of TMEM (warps w and
-  //     w+4 read lanes 32(w%4).. = weight rows of this CTA and split the NR
-  //     columns) into the receive buffer of the cluster rank owning the
-  //     activation row: rcv[k][row - rows_per*owner][128], k = this CTA's
-  //     rank (K split), each owner holding rows_per = ceil(NR / ks) rows.
-  //     Stores to other ranks go through distributed shared memory.
-  // (2) cluster barrier: every partial tile has landed.
-  // (3) all warps: each owner sums its rows over the K splits in rank order
-  //     (deterministic) and applies the Epi store for 4 adjacent weight rows
-  //     per thread, as one 16- or 8-byte vector where the layout allows.
-  // The receive buffer reuses the stage ring; with ks > 1 a first cluster
-  // barrier makes sure no CTA of the cluster still reads its stages.
+  // (1) warps 0-15 move the fp32 accumulator tile out of TMEM (warp w reads
+  //     lanes 32(w%4).. = weight rows of this CTA, the four warps of a lane
+  //     quarter split the NR columns) into a [NR][128] partial tile: in
+  //     shared memory (the stage ring, free once DONE has fired) when K is
+  //     not split, else in this CTA's slice of the split-K workspace in
+  //     global memory (L2-resident; distributed shared memory moved such
+  //     tiles at a fraction of L2's per-SM bandwidth).
+  // (2) barrier (CTA, or cluster: release / acquire at cluster scope, so the
+  //     partial tiles written to global memory are visible to the cluster).
+  // (3) all warps: each cluster rank owns rows_per = ceil(NR / ks) activation
+  //     rows, sums them over the K splits in rank order (deterministic) and
+  //     applies the Epi store for 4 adjacent weight rows per thread, as one
+  //     16- or 8-byte vector where the layout allows.
+  // Weight-row constants of the store (biases are model data: read before
+  // the dependency wait)
+  const int n0 = tile0 * 16 + 4 * lane;  // weight rows n0 .. n0+3
+  const int nvalid = max(0, min(4, e.N - n0));
+  float b4[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) b4[i] = i < nvalid ? tc_epi_bias(e, n0 + i) : 0.f;
   pdl_wait();  // (returned long ago for the activation loader)
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = ks > 1 ? (int)cluster.block_rank() : 0;
   const int rows_per = (NR + ks - 1) / ks;
-  float* rcv = reinterpret_cast<float*>(sm);
+  // partial tiles of this cluster: [ks][NR][128] fp32
+  float* part = ks > 1 ? e.split_ws + (size_t)(blockIdx.y * gridDim.x + blockIdx.x) * ks * NR * 128
+                       : reinterpret_cast<float*>(sm);
   bool done_ok = true;
   if (warp < TC_DQ_WARPS) {
     done_ok = mbar_wait(DONE, 0, abort_flag, 6, &g_tc_error);
     done_ok = __all_sync(0xffffffffu, done_ok);
   }
-  if (ks > 1) cluster.sync();
   if (warp < TC_DQ_WARPS && done_ok) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const int f = (warp & 3) * 32 + lane;
-    const int nchunk = NR / 16, part = (nchunk + 3) / 4, sub = warp >> 2;
-    const int cbeg = min(nchunk, sub * part), cend = min(nchunk, cbeg + part);
+    const int nchunk = NR / 16, qpart = (nchunk + 3) / 4, sub = warp >> 2;
+    const int cbeg = min(nchunk, sub * qpart), cend = min(nchunk, cbeg + qpart);
+    float* mine = part + (size_t)crank * NR * 128;
     for (int ci = cbeg; ci < cend; ci++) {
       const int c0 = ci * 16;
       uint32_t v[16];
@@ -466,28 +501,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
           : "r"(taddr));
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      int owner = c0 / rows_per, rem = c0 - owner * rows_per;
-      float* dst = owner == crank ? rcv : cluster.map_shared_rank(rcv, owner);
 #pragma unroll
-      for (int i = 0; i < 16; i++) {
-        dst[((size_t)crank * rows_per + rem) * 128 + f] = __uint_as_float(v[i]);
-        if (++rem == rows_per && i < 15) {
-          rem = 0;
-          owner++;
-          dst = owner == crank ? rcv : cluster.map_shared_rank(rcv, owner);
-        }
-      }
+      for (int i = 0; i < 16; i++) mine[(size_t)(c0 + i) * 128 + f] = __uint_as_float(v[i]);
     }
   }
   if (ks > 1) cluster.sync();
   else __syncthreads();
   if (*abort_flag == 0) {
-    const int n0 = tile0 * 16 + 4 * lane;  // weight rows n0 .. n0+3
-    const int nvalid = max(0, min(4, e.N - n0));
     const TcEpiRow er = tc_epi_row(e, n0);
-    float b4[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) b4[i] = i < nvalid ? tc_epi_row(e, n0 + i).bias : 0.f;
     const bool qkv_q = e.mode == EPI_QKV && n0 < e.d;
     // the 4 weight rows are adjacent in the output unless a head of a
     // cache layout ends inside the quad
@@ -498,12 +519,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int r = r0 + row_lo + jr;
       if (r >= R) break;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int k = 0; k < ks; k++) {  // rank order
-        const float4 p4 = reinterpret_cast<const float4*>(rcv + ((size_t)k * rows_per + jr) * 128)[lane];
-        acc.x += p4.x;
-        acc.y += p4.y;
-        acc.z += p4.z;
-        acc.w += p4.w;
+      if (ks > 1) {
+        for (int k = 0; k < ks; k++) {  // rank order
+          const float4 p4 = __ldcg(reinterpret_cast<const float4*>(part + ((size_t)k * NR + row_lo + jr) * 128) + lane);
+          acc.x += p4.x;
+          acc.y += p4.y;
+          acc.z += p4.z;
+          acc.w += p4.w;
+        }
+      } else {
+        acc = reinterpret_cast<const float4*>(part + (size_t)jr * 128)[lane];
       }
       const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
       if (!contig) {
@@ -566,8 +591,6 @@ int launch_tc_t(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cu
     const int per = (nk + ks - 1) / ks;
     ks = (nk + per - 1) / per;  // every split gets >= 1 stage
   }
-  // the epilogue's receive buffer [ks][ceil(NR/ks)][128] fp32 reuses the stage ring
-  while (ks > 1 && (uint32_t)ks * ((NR + ks - 1) / ks) * 512u > L.bar0) ks--;
   if (ks > 1) {
     // keep every cluster of the grid co-resident (one wave)
     static thread_local int cached_dev = -1, cached_nr = -1, cached_ks = -1, cached_max = 0;
@@ -598,6 +621,11 @@ int launch_tc_t(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cu
       }
       if (maxc >= groups * rtiles) break;
     }
+  }
+  if (ks > 1 && (!e.split_ws || (int64_t)groups * rtiles * ks * NR * 128 > e.split_ws_floats)) {
+    set_error("tcgen05 GEMM: split-K workspace missing or too small (%lld floats needed)",
+              (long long)groups * rtiles * ks * NR * 128);
+    return WG_ERR_INVALID;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(groups, rtiles, ks);

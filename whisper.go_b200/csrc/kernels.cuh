@@ -35,7 +35,16 @@ struct Epi {
   const float* bias_q = nullptr;     // QKV q bias [d]
   const float* bias_v = nullptr;     // QKV v bias [d]; CROSS: [L][d]
   int U = 0;                         // CROSS: utterances
+  // tcgen05 path with K split over a cluster: partial tiles of the splits,
+  // device memory of at least TC_SPLIT_WS_FLOATS floats, owned by the stream
+  // (no other launch may use it concurrently); contents need no initialisation
+  float* split_ws = nullptr;
+  int64_t split_ws_floats = 0;
 };
+
+// Upper bound of the split-K workspace: at most one wave of 148 CTAs, each
+// with a 128 x 256 fp32 partial tile (19.4 MB).
+constexpr int64_t TC_SPLIT_WS_FLOATS = 148LL * 256 * 128;
 
 // path: 0 auto, 1 small-R kernel (mma.sync GEMV), 2 large-R mma.sync kernel,
 // 3 tcgen05 tensor-core kernel (quantised weights, K % 64 == 0).

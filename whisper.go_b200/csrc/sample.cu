@@ -62,6 +62,10 @@ __device__ __forceinline__ ArgMax warp_argmax(ArgMax a) {
   return a;
 }
 
+// Logit rows are scanned with SCAN_UNROLL independent loads in flight per
+// thread (a row is 51,866 floats; one load at a time made the scan latency-bound).
+constexpr int SCAN_UNROLL = 8;
+
 // ---- greedy ----------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) greedy_kernel(SampleState s) {
   pdl_trigger();
@@ -71,10 +75,22 @@ __global__ void __launch_bounds__(1024) greedy_kernel(SampleState s) {
   penalty_row(s, r);
   const float* lg = s.logits + (int64_t)r * s.V;
   ArgMax all{-INFINITY, -1}, excl{-INFINITY, -1};
-  for (int i = threadIdx.x; i < s.V; i += blockDim.x) {
-    float v = __fmul_rn(lg[i], s.inv_temp);
-    all = better(all, ArgMax{v, i});
-    if (i != s.eot) excl = better(excl, ArgMax{v, i});
+  // each thread visits i = tid, tid + blockDim, ... in increasing order; the
+  // loads of SCAN_UNROLL visits are issued before any is used
+  const int stride = blockDim.x;
+  for (int i0 = threadIdx.x; i0 < s.V; i0 += SCAN_UNROLL * stride) {
+    float x[SCAN_UNROLL];
+#pragma unroll
+    for (int k = 0; k < SCAN_UNROLL; k++) x[k] = i0 + k * stride < s.V ? lg[i0 + k * stride] : 0.f;
+#pragma unroll
+    for (int k = 0; k < SCAN_UNROLL; k++) {
+      const int i = i0 + k * stride;
+      if (i < s.V) {
+        const float v = __fmul_rn(x[k], s.inv_temp);
+        all = better(all, ArgMax{v, i});
+        if (i != s.eot) excl = better(excl, ArgMax{v, i});
+      }
+    }
   }
   __shared__ ArgMax red[2][32];
   all = warp_argmax(all);
@@ -115,17 +131,34 @@ __global__ void __launch_bounds__(1024) greedy_kernel(SampleState s) {
 // ---- beam: per-row top-5 of log_softmax(logits / T) ----------------------------
 constexpr int TOPK = 5;
 
-__device__ __forceinline__ void top_insert(float* v, int* ix, float nv, int ni) {
-  // keep v[0..4] sorted: larger first, lower index first on ties
+__device__ __forceinline__ void top_insert(float (&v)[TOPK], int (&ix)[TOPK], float nv, int ni) {
+  // keep v[0..4] sorted: larger first, lower index first on ties. The new
+  // entry replaces the last one and bubbles up; every index is a constant,
+  // so the list stays in registers.
   if (!(nv > v[TOPK - 1] || (nv == v[TOPK - 1] && ni < ix[TOPK - 1] && ix[TOPK - 1] >= 0))) return;
-  int j = TOPK - 1;
-  while (j > 0 && (nv > v[j - 1] || (nv == v[j - 1] && ni < ix[j - 1]))) {
-    v[j] = v[j - 1];
-    ix[j] = ix[j - 1];
-    j--;
+  v[TOPK - 1] = nv;
+  ix[TOPK - 1] = ni;
+#pragma unroll
+  for (int j = TOPK - 1; j > 0; j--) {
+    if (v[j] > v[j - 1] || (v[j] == v[j - 1] && ix[j] < ix[j - 1])) {
+      const float tv = v[j];
+      const int ti = ix[j];
+      v[j] = v[j - 1];
+      ix[j] = ix[j - 1];
+      v[j - 1] = tv;
+      ix[j - 1] = ti;
+    }
   }
-  v[j] = nv;
-  ix[j] = ni;
+}
+// Drops the head of a sorted list (the rest moves up one place).
+__device__ __forceinline__ void top_pop(float (&v)[TOPK], int (&ix)[TOPK]) {
+#pragma unroll
+  for (int j = 0; j + 1 < TOPK; j++) {
+    v[j] = v[j + 1];
+    ix[j] = ix[j + 1];
+  }
+  v[TOPK - 1] = -INFINITY;
+  ix[TOPK - 1] = -1;
 }
 
 constexpr int TOPK_THREADS = 512;  // one wave of rows (four CTAs per SM)
@@ -144,10 +177,20 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(SampleState s) {
 #pragma unroll
   for (int j = 0; j < TOPK; j++) { tv[j] = -INFINITY; ti[j] = -1; }
   float mx = -INFINITY;
-  for (int i = threadIdx.x; i < s.V; i += blockDim.x) {
-    float v = __fmul_rn(lg[i], s.inv_temp);
-    mx = fmaxf(mx, v);
-    top_insert(tv, ti, v, i);
+  const int stride = blockDim.x;
+  for (int i0 = threadIdx.x; i0 < s.V; i0 += SCAN_UNROLL * stride) {
+    float x[SCAN_UNROLL];
+#pragma unroll
+    for (int k = 0; k < SCAN_UNROLL; k++) x[k] = i0 + k * stride < s.V ? lg[i0 + k * stride] : 0.f;
+#pragma unroll
+    for (int k = 0; k < SCAN_UNROLL; k++) {
+      const int i = i0 + k * stride;
+      if (i < s.V) {
+        const float v = __fmul_rn(x[k], s.inv_temp);
+        mx = fmaxf(mx, v);
+        top_insert(tv, ti, v, i);
+      }
+    }
   }
   __shared__ float cv[32 * TOPK];
   __shared__ int ci[32 * TOPK];
@@ -155,11 +198,10 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(SampleState s) {
   __shared__ float smax;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   // warp merge: 5 rounds of arg-max over the lanes' list heads
-  int head = 0;
   for (int k = 0; k < TOPK; k++) {
-    ArgMax a{head < TOPK ? tv[head] : -INFINITY, head < TOPK ? ti[head] : -1};
-    ArgMax b = warp_argmax(a);
-    if (a.i == b.i && b.i >= 0) head++;
+    const ArgMax a{tv[0], ti[0]};
+    const ArgMax b = warp_argmax(a);
+    if (a.i == b.i && b.i >= 0) top_pop(tv, ti);
     if (lane == 0) { cv[warp * TOPK + k] = b.v; ci[warp * TOPK + k] = b.i; }
   }
   float m = warp_max(mx);
@@ -176,7 +218,14 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(SampleState s) {
   // terms in float32 (expf, within 2 ulp of the rounded float64 value: the
   // reference's sequential float32 sum is reordered here anyway)
   float es = 0.f;
-  for (int i = threadIdx.x; i < s.V; i += blockDim.x) es += expf(__fsub_rn(__fmul_rn(lg[i], s.inv_temp), mx));
+  for (int i0 = threadIdx.x; i0 < s.V; i0 += SCAN_UNROLL * stride) {
+    float x[SCAN_UNROLL];
+#pragma unroll
+    for (int k = 0; k < SCAN_UNROLL; k++) x[k] = i0 + k * stride < s.V ? lg[i0 + k * stride] : 0.f;
+#pragma unroll
+    for (int k = 0; k < SCAN_UNROLL; k++)
+      if (i0 + k * stride < s.V) es += expf(__fsub_rn(__fmul_rn(x[k], s.inv_temp), mx));
+  }
   es = warp_sum(es);
   __syncthreads();
   if (lane == 0) wsum[warp] = es;
@@ -196,13 +245,13 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(SampleState s) {
     lv[j] = ok ? cv[lane * TOPK + j] : -INFINITY;
     li[j] = ok ? ci[lane * TOPK + j] : -1;
   }
-  head = 0;
   float fv[TOPK];
   int fi[TOPK];
+#pragma unroll
   for (int k = 0; k < TOPK; k++) {
-    ArgMax a{head < TOPK ? lv[head] : -INFINITY, head < TOPK ? li[head] : -1};
-    ArgMax b = warp_argmax(a);
-    if (a.i == b.i && b.i >= 0) head++;
+    const ArgMax a{lv[0], li[0]};
+    const ArgMax b = warp_argmax(a);
+    if (a.i == b.i && b.i >= 0) top_pop(lv, li);
     fv[k] = b.v;
     fi[k] = b.i;
   }
