@@ -188,7 +188,8 @@ int wg_teacher_forced_logits(wg_model* m, const float* const* enc, int U, int T_
  * (gguf/dequant.go:92-201). out: n fp32 values. Bit-exact with the reference. */
 int wg_dequant_test(uint32_t qtype, const void* raw, int64_t n, float* out);
 /* out[m, rows] = x[m, cols] * dequant(W[rows, cols])^T with the device GEMV
- * (path 0: auto, 1: SIMT GEMV, 2: tcgen05 tensor-core tiles).
+ * (path 0: auto, 1: small-batch mma.sync GEMV, 2: mma.sync tiles,
+ * 3: tcgen05 tensor-core kernel). x is rounded to f16 on the device first.
  * Replaces ml.MatMulQuantTransBInto (ml/matmul_q8.go:93-119). */
 int wg_matmul_test(uint32_t qtype, const void* raw, int rows, int cols,
                    const float* x, int m, float* out, int path);
