@@ -194,6 +194,37 @@ int wg_dequant_test(uint32_t qtype, const void* raw, int64_t n, float* out);
 int wg_matmul_test(uint32_t qtype, const void* raw, int rows, int cols,
                    const float* x, int m, float* out, int path);
 
+/* ---- allocation-free matmul (no reference counterpart) --------------------
+ * For callers that may not allocate device memory once they are running
+ * (their own pool owns the device, or an allocation would stall a
+ * latency-critical path): out[r][n] = sum_k W[n][k] * x16[r][k] for one
+ * uploaded weight matrix of replica `replica` of m, on the tcgen05 tensor-core
+ * kernel, enqueued on `stream` (a cudaStream_t; NULL is the default stream).
+ * No bias is added. This call allocates no device memory: when the kernel
+ * splits K over a cluster, its partial tiles go to a fixed scratch array that
+ * is part of the library's device image (WG_NOALLOC_SCRATCH_FLOATS floats,
+ * 8 MiB, per device); a shape that needs more is rejected with
+ * WG_ERR_INVALID and the error text gives the floats it needs. Nothing in
+ * the scratch has to start at zero.
+ *   which : 0 self-attention q|k|v (N = 3d, K = d), 1 self-attention out,
+ *           2 cross-attention q, 3 cross-attention out (N = K = d),
+ *           4 mlp.0 (N = 4d, K = d), 5 mlp.2 (N = d, K = 4d)
+ *   x16   : device f16 [rows][ldx], 16-byte aligned, ldx % 8 == 0, ldx >= K
+ *   out   : device fp32 [rows][ldo], ldo >= N
+ *   wait  : nonzero: wait for the stream and report a CUDA error or an
+ *           expired device-side wait (WG_ERR_DEVICE_FLAG) before returning;
+ *           zero: return once the kernel is enqueued.
+ * The first call on a device also does set-up (it looks up the scratch
+ * array's device address with that device current), so make it before any
+ * stream capture begins. All calls on one device share the scratch: calls
+ * whose kernels can overlap in time (different streams or host threads)
+ * race and give wrong results; issue them in one stream or one at a time.
+ * The caller's current device is restored before returning. */
+#define WG_NOALLOC_SCRATCH_FLOATS (2LL * 1024 * 1024)
+int wg_model_matmul_noalloc(wg_model* m, int replica, int layer, int which,
+                            const void* x16, int ldx, int rows, float* out, int ldo,
+                            void* stream, int wait);
+
 /* ---- measurement hooks used by bench.py ---------------------------------- */
 enum {
   WG_KCLASS_GEMV = 0,        /* the 6 weight matmuls of every layer */

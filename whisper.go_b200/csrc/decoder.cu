@@ -14,6 +14,7 @@
 #include <cstdarg>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <thread>
 #include <vector>
@@ -1098,3 +1099,91 @@ int wg_job_time_kernel(wg_job* J, int kclass, int iters, double* ms, double* byt
 }
 
 }  // extern "C"
+
+// ---- allocation-free matmul ------------------------------------------------------
+// wg_model_matmul_noalloc runs the tcgen05 GEMM on a model's uploaded weights
+// with caller-owned activations and outputs, and takes the split-K scratch
+// from this fixed array instead of allocating a workspace: it exists for
+// callers that may not allocate device memory while they run. The array is
+// part of the module's device image (one copy per device); its address is
+// looked up once per device with that device current. Every call on a device
+// shares it, so calls whose kernels overlap in time race.
+namespace wg {
+static __device__ __align__(256) float g_noalloc_scratch[WG_NOALLOC_SCRATCH_FLOATS];
+namespace {
+constexpr int NOALLOC_MAX_DEV = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[NOALLOC_MAX_DEV] = {};
+
+// Device address of the scratch array on device dev (which must be current).
+int noalloc_scratch(int dev, float** out) {
+  if (dev < 0 || dev >= NOALLOC_MAX_DEV) {
+    set_error("wg_model_matmul_noalloc: device %d out of range", dev);
+    return WG_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    float* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress((void**)&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      set_error("wg_model_matmul_noalloc: cudaGetSymbolAddress of the scratch array failed: %s",
+                cudaGetErrorString(e));
+      return WG_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return WG_OK;
+}
+}  // namespace
+}  // namespace wg
+
+extern "C" int wg_model_matmul_noalloc(wg_model* m, int replica, int layer, int which, const void* x16, int ldx,
+                                       int rows, float* out, int ldo, void* stream, int wait) {
+  using namespace wg;
+  if (!m || replica < 0 || replica >= (int)m->devs.size() || layer < 0 || layer >= m->L || which < 0 ||
+      which > 5 || !x16 || !out || rows <= 0) {
+    set_error("wg_model_matmul_noalloc: bad argument");
+    return WG_ERR_INVALID;
+  }
+  DevModel& dm = *m->devs[replica];
+  const DevLayer& ly = dm.layers[layer];
+  const DMat* mats[6] = {&ly.qkv, &ly.so, &ly.cq, &ly.co, &ly.m0, &ly.m2};
+  const DMat& W = *mats[which];
+  if (!tc_supported(W)) {
+    set_error("wg_model_matmul_noalloc: the tensor-core kernel needs a quantised matrix with K %% 64 == 0");
+    return WG_ERR_UNSUPPORTED;
+  }
+  if (ldx < W.cols || ldx % 8 || (reinterpret_cast<uintptr_t>(x16) & 15) || ldo < W.rows) {
+    set_error("wg_model_matmul_noalloc: x16 needs 16-byte aligned rows of ldx >= %d (ldx %% 8 == 0), out ldo >= %d",
+              W.cols, W.rows);
+    return WG_ERR_INVALID;
+  }
+  int prev = -1;
+  WG_CHECK_CUDA(cudaGetDevice(&prev));
+  WG_CHECK_CUDA(cudaSetDevice(dm.dev));
+  float* ws = nullptr;
+  int rc = noalloc_scratch(dm.dev, &ws);
+  if (rc == WG_OK) {
+    Epi e;
+    e.mode = EPI_F32;
+    e.out = out;
+    e.ldo = ldo;
+    e.N = W.rows;
+    e.split_ws = ws;
+    e.split_ws_floats = WG_NOALLOC_SCRATCH_FLOATS;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    rc = launch_matmul(W, reinterpret_cast<const __half*>(x16), ldx, rows, e, st, 3);
+    if (rc == WG_ERR_INVALID) {
+      const std::string why = last_error();
+      set_error("wg_model_matmul_noalloc: %s; the static scratch holds %lld floats", why.c_str(),
+                (long long)WG_NOALLOC_SCRATCH_FLOATS);
+    }
+    if (rc == WG_OK && wait) {
+      rc = wait_stream(st);
+      if (rc == WG_OK) rc = check_wait_flags();
+    }
+  }
+  cudaSetDevice(prev);
+  return rc;
+}

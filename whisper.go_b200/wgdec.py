@@ -121,6 +121,9 @@ def _declare(lib):
                                           ctypes.c_int, c_float_p, ctypes.c_int]),
         "wg_job_time_kernel": (ctypes.c_int, [P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_double),
                                               ctypes.POINTER(ctypes.c_double)]),
+        "wg_model_matmul_noalloc": (ctypes.c_int, [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                                   ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                                   ctypes.c_void_p, ctypes.c_int]),
     }
     for name, (res, args) in sig.items():
         f = getattr(lib, name)
