@@ -47,6 +47,13 @@ constexpr int TC_XLOAD_WARP = 17; // activation TMA loader
 constexpr int TC_WLOAD_WARP = 18; // weight bulk-copy loader
 constexpr int TC_THREADS = 19 * 32;
 constexpr int TC_DQ_NS = 6;       // weight stages in flight (raw ring depth)
+// Lanes issuing copies in each loader warp (stage kl from lane kl % lanes).
+// The copies of an SM share its L2 ingest (~110-120 GB/s); with one lane they
+// complete in stage order, which is the order the pipeline consumes them,
+// while several lanes make the stages in flight share the bandwidth and each
+// one land later. Measured: 1 lane is fastest for these GEMMs.
+constexpr int TC_LOAD_LANES = 1;
+static_assert(TC_LOAD_LANES <= TC_DQ_NS, "a loader lane must never wait for a slot of its own round");
 __device__ int g_tc_error;  // first expired wait: (stage << 8) | role
 
 // K-major, 128B-swizzled canonical operand (8-row atoms of 1024 B).
@@ -100,7 +107,8 @@ __host__ __device__ inline TcLayout tc_layout(uint32_t qt, int NR) {
   L.b0 = 0;
   L.raw0 = L.b0 + L.stages * L.b_bytes;
   L.bar0 = L.raw0 + raw;
-  L.total = L.bar0 + 8 * (2 * TC_S_MAX + 2 * TC_DQ_NS + 1) + 16 + 1024;  // barriers, tmem slot, slack
+  // barriers, abort flag + tmem slot, drain bookkeeping per ring slot, slack
+  L.total = L.bar0 + 8 * (2 * TC_S_MAX + 2 * TC_DQ_NS + 1) + 16 + 4 * (2 * TC_S_MAX + TC_DQ_NS) + 1024;
   return L;
 }
 
@@ -258,6 +266,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint32_t DONE = bar + 8 * NBAR;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L.bar0 + 8 * (NBAR + 1));
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + L.bar0 + 8 * (NBAR + 1) + 4);
+  // Drain bookkeeping: last stage whose copy was issued into each activation /
+  // weight ring slot (-1: none) and the dequant arrivals made on each FULL[s]
+  // so far; after an abort the copies still in flight are waited for.
+  volatile int* issued_x = reinterpret_cast<volatile int*>(sm + L.bar0 + 8 * (NBAR + 1) + 16);
+  volatile int* issued_w = issued_x + TC_S_MAX;
+  int* dq_arrivals = const_cast<int*>(issued_w + TC_DQ_NS);
   constexpr int pb = QT == WG_QTYPE_Q8_0 ? 16 : 8;
   constexpr bool has_m = QT == WG_QTYPE_Q4_1 || QT == WG_QTYPE_Q5_1;
   constexpr bool has_h = QT == WG_QTYPE_Q5_0 || QT == WG_QTYPE_Q5_1;
@@ -274,23 +288,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     bulk_g2s(dst + qs_b, W.dsc + g0 * 8, 512, RAW_FULL(s));
     if (has_m) bulk_g2s(dst + qs_b + 512, W.msc + g0 * 8, 512, RAW_FULL(s));
     if (has_h) bulk_g2s(dst + qs_b + 1024, W.hb + g0 * 32, 1024, RAW_FULL(s));
+    issued_w[s] = kl;
   };
   // The weight loader initialises the RAW ring's barriers itself and issues
   // the ring's first stages at once (their slots are free), so the weight
   // stream overlaps the TMEM allocation and the block barrier below.
   const int n_pre = min(nk, TC_DQ_NS);
-  if (warp == TC_WLOAD_WARP && lane == 0) {
-    for (int s = 0; s < TC_DQ_NS; s++) {
-      mbar_init(RAW_FULL(s), 1);
-      mbar_init(RAW_EMPTY(s), 8);
+  if (warp == TC_WLOAD_WARP) {
+    if (lane == 0) {
+      for (int s = 0; s < TC_DQ_NS; s++) {
+        mbar_init(RAW_FULL(s), 1);
+        mbar_init(RAW_EMPTY(s), 8);
+        issued_w[s] = -1;
+      }
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    for (int kl = 0; kl < n_pre; kl++) issue_weights(kl);
+    __syncwarp();
+    if (lane == 0)
+      for (int kl = 0; kl < n_pre; kl++) issue_weights(kl);
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; s++) {
       mbar_init(FULL(s), 8 + 1);
       mbar_init(EMPTY(s), 1);
+      issued_x[s] = -1;
+      dq_arrivals[s] = 0;
     }
     mbar_init(DONE, 1);
     *abort_flag = 0;
@@ -309,26 +331,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == TC_WLOAD_WARP) {
-    if (lane == 0) {
-      // ---------------- weight loader: the remaining stages ----------------
-      for (int kl = n_pre; kl < nk; kl++) {
+    // ---------------- weight loader: the remaining stages ----------------
+    // (TC_LOAD_LANES <= TC_DQ_NS: a lane only waits for slots that stages
+    // issued in earlier rounds occupy)
+    for (int k0 = n_pre; k0 < nk; k0 += TC_LOAD_LANES) {
+      const int kl = k0 + lane;
+      bool ok = true;
+      if (lane < TC_LOAD_LANES && kl < nk) {
         const int s = kl % TC_DQ_NS;
         const uint32_t ph = (uint32_t)(kl / TC_DQ_NS) & 1u;
-        if (!mbar_wait(RAW_EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 1, &g_tc_error)) break;
-        issue_weights(kl);
+        ok = mbar_wait(RAW_EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 1, &g_tc_error);
+        if (ok) issue_weights(kl);
       }
+      if (!__all_sync(0xffffffffu, ok)) break;
     }
   } else if (warp == TC_XLOAD_WARP) {
-    if (lane == 0) {
-      // ---------------- activation loader ----------------
-      pdl_wait();
-      for (int kl = 0; kl < nk; kl++) {
+    // ---------------- activation loader ----------------
+    pdl_wait();
+    const int lanes = min(TC_LOAD_LANES, S);
+    for (int k0 = 0; k0 < nk; k0 += lanes) {
+      const int kl = k0 + lane;
+      bool ok = true;
+      if (lane < lanes && kl < nk) {
         const int s = kl % S;
         const uint32_t ph = (uint32_t)(kl / S) & 1u;
-        if (!mbar_wait(EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 2, &g_tc_error)) break;
-        mbar_arrive_tx(FULL(s), L.b_bytes);
-        tma_2d(base + L.b0 + s * L.b_bytes, &xmap, kstage(kl) * TC_BK, r0, FULL(s));
+        ok = mbar_wait(EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 2, &g_tc_error);
+        if (ok) {
+          mbar_arrive_tx(FULL(s), L.b_bytes);
+          tma_2d(base + L.b0 + s * L.b_bytes, &xmap, kstage(kl) * TC_BK, r0, FULL(s));
+          issued_x[s] = kl;
+        }
       }
+      if (!__all_sync(0xffffffffu, ok)) break;
     }
   } else if (warp == TC_MMA_WARP) {
     if (lane == 0) {
@@ -448,6 +482,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (lane == 0) {
         mbar_arrive(RAW_EMPTY(rs));
         mbar_arrive(FULL(s));
+        atomicAdd(&dq_arrivals[s], 1);
       }
     }
   }
@@ -551,6 +586,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
+  if (*abort_flag) {
+    // a wait expired: let the copies still in flight land (bounded) before
+    // the CTA's shared memory is released; at most one per ring slot, the last
+    // activation slot s: the phase of its last copy, p = kl / S, completes
+    // once its 8 dequant arrivals and the bytes are in; arrivals the dequant
+    // warps did not make (they stopped) are made here, no warp runs any more
+    if (warp == TC_XLOAD_WARP && lane < S && issued_x[lane] >= 0) {
+      const int p = issued_x[lane] / S;
+      for (int i = dq_arrivals[lane] - 8 * p; i < 8; i++) mbar_arrive(FULL(lane));
+      mbar_drain(FULL(lane), (uint32_t)p & 1u);
+    }
+    if (warp == TC_WLOAD_WARP && lane < TC_DQ_NS && issued_w[lane] >= 0)
+      mbar_drain(RAW_FULL(lane), (uint32_t)(issued_w[lane] / TC_DQ_NS) & 1u);
+  }
   if (warp == TC_MMA_WARP) {
     __syncwarp();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
