@@ -63,7 +63,8 @@ def _close(gpu, ref):
 
 
 @pytest.mark.parametrize("qt", QT)
-@pytest.mark.parametrize("R,path", [(1, 1), (5, 1), (8, 1), (13, 1), (16, 1), (16, 2), (40, 2), (130, 2), (5, 2)])
+@pytest.mark.parametrize("R,path", [(1, 1), (5, 1), (8, 1), (13, 1), (16, 1), (16, 2), (40, 2), (130, 2), (5, 2),
+                                    (1, 4), (5, 4), (16, 4)])
 def test_matmul_vs_oracle(qt, R, path):
     raw, a, ref = _matmul_case(qt, R, 200, 256, seed=R * 7 + path)
     gpu = wgdec.matmul(qt, raw, 200, 256, a, path=path)
@@ -83,6 +84,18 @@ def test_matmul_tcgen05_vs_oracle(qt, R):
 def test_matmul_tcgen05_model_shapes(R, rows, K):
     raw, a, ref = _matmul_case("Q8_0", R, rows, K, seed=R + K)
     gpu = wgdec.matmul("Q8_0", raw, rows, K, a, path=3)
+    assert _close(gpu, ref), float(np.max(np.abs(gpu - ref)))
+
+
+@pytest.mark.parametrize("qt", ["Q8_0", "Q5_1"])
+@pytest.mark.parametrize("R,rows,K", [(5, 1280, 5120), (1, 3840, 1280), (16, 5120, 1280), (5, 1300, 1280),
+                                      (3, 2000, 768)])
+def test_matmul_small_batch_model_shapes(qt, R, rows, K):
+    """The small-batch GEMV (path 1: a 128-row weight group per CTA, K ranges
+    summed across a thread-block cluster) at decoder shapes, with partial
+    weight groups and K split into up to 8 ranges."""
+    raw, a, ref = _matmul_case(qt, R, rows, K, seed=R + rows + K)
+    gpu = wgdec.matmul(qt, raw, rows, K, a, path=1)
     assert _close(gpu, ref), float(np.max(np.abs(gpu - ref)))
 
 

@@ -154,6 +154,11 @@ static int check_wait_flags() {
     set_error("an attention kernel's bounded wait expired (code 0x%x)", w);
     return WG_ERR_DEVICE_FLAG;
   }
+  WG_CHECK(gemv_error_word(&w, true));
+  if (w) {
+    set_error("a GEMV kernel's bounded wait expired (code 0x%x)", w);
+    return WG_ERR_DEVICE_FLAG;
+  }
   return WG_OK;
 }
 
@@ -201,6 +206,7 @@ int build_devmodel(const wg_model_desc* md, int dev, DevModel** out) {
   if ((rc = init_gemm_attributes()) != WG_OK) return fail(rc);
   if ((rc = init_attn_attributes()) != WG_OK) return fail(rc);
   if ((rc = init_tc_attributes()) != WG_OK) return fail(rc);
+  if ((rc = init_gemv_bulk_attributes()) != WG_OK) return fail(rc);
   const int d = md->n_state, L = md->n_layer, ctx = md->n_text_ctx;
   // fp32 vectors: 6 LN + 7 biases (d or 4d) per layer, final LN, pos emb, cross V bias
   std::vector<float> host;
@@ -962,6 +968,7 @@ int wg_matmul_test(uint32_t qtype, const void* raw, int rows, int cols, const fl
   WG_CHECK_CUDA(cudaSetDevice(0));
   WG_CHECK(init_gemm_attributes());
   WG_CHECK(init_tc_attributes());
+  WG_CHECK(init_gemv_bulk_attributes());
   cudaStream_t st = nullptr;
   WG_CHECK_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
   wg_matrix wm{qtype, rows, cols, raw};

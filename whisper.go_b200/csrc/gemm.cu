@@ -15,31 +15,11 @@
 //     shared-memory reduction across warps.
 //   large-R kernel (R > 16): 64 weight rows x 64 activation rows per CTA,
 //     activation K-slices through a 4-stage cp.async ring.
-#include "kernels.cuh"
+#include "gemv_frag.cuh"
 
 namespace wg {
 namespace {
 
-__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint4 ldg_stream16(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-__device__ __forceinline__ uint2 ldg_stream8(const void* p) {
-  uint2 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-  return v;
-}
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
   uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
@@ -47,117 +27,6 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
-
-__device__ __forceinline__ uint32_t h2_as_u32(__half2 h) {
-  uint32_t u;
-  memcpy(&u, &h, 4);
-  return u;
-}
-__device__ __forceinline__ __half2 u32_as_h2(uint32_t u) {
-  __half2 h;
-  memcpy(&h, &u, 4);
-  return h;
-}
-
-// One lane's share of one (tile, block).
-struct Pay {
-  uint4 q;
-  uint32_t hb;
-  __half2 d, m;
-};
-
-template <uint32_t QT>
-__device__ __forceinline__ Pay load_payload(const DMat& W, int64_t slot, int lane) {
-  Pay p;
-  if (QT == WG_QTYPE_Q8_0) {
-    p.q = ldg_stream16(W.qs + (slot * 32 + lane) * 16);
-  } else {
-    uint2 v = ldg_stream8(W.qs + (slot * 32 + lane) * 8);
-    p.q = make_uint4(v.x, v.y, 0, 0);
-  }
-  p.d = W.dsc[slot * 8 + (lane >> 2)];
-  if (QT == WG_QTYPE_Q4_1 || QT == WG_QTYPE_Q5_1) p.m = W.msc[slot * 8 + (lane >> 2)];
-  else p.m = __float2half2_rn(0.f);
-  if (QT == WG_QTYPE_Q5_0 || QT == WG_QTYPE_Q5_1) p.hb = W.hb[slot * 32 + lane];
-  else p.hb = 0;
-  return p;
-}
-
-// A fragment of mma step s (0/1) of a 32-wide quant block.
-// reg 0: row g, k 2t..2t+1; reg 1: row g+8; reg 2: row g, k+8; reg 3: row g+8, k+8.
-template <uint32_t QT>
-__device__ __forceinline__ void dequant_step(const Pay& p, int s, uint32_t* a) {
-  const __half2 dg = __low2half2(p.d), dg8 = __high2half2(p.d);
-  if (QT == WG_QTYPE_Q8_0) {
-    uint32_t w0 = (s ? p.q.z : p.q.x) ^ 0x80808080u;
-    uint32_t w1 = (s ? p.q.w : p.q.y) ^ 0x80808080u;
-    const __half2 bias = __float2half2_rn(1152.f);  // 1024 + 128
-    __half2 h0 = __hsub2(u32_as_h2(__byte_perm(w0, 0x64, 0x4140)), bias);
-    __half2 h1 = __hsub2(u32_as_h2(__byte_perm(w0, 0x64, 0x4342)), bias);
-    __half2 h2 = __hsub2(u32_as_h2(__byte_perm(w1, 0x64, 0x4140)), bias);
-    __half2 h3 = __hsub2(u32_as_h2(__byte_perm(w1, 0x64, 0x4342)), bias);
-    a[0] = h2_as_u32(__hmul2(h0, dg));
-    a[1] = h2_as_u32(__hmul2(h1, dg8));
-    a[2] = h2_as_u32(__hmul2(h2, dg));
-    a[3] = h2_as_u32(__hmul2(h3, dg8));
-  } else {
-    uint32_t w = s ? p.q.y : p.q.x;
-#pragma unroll
-    for (int r = 0; r < 4; r++) {
-      uint32_t hq = ((w >> (4 * r)) & 0x000F000Fu) | 0x64006400u;
-      if (QT == WG_QTYPE_Q5_0 || QT == WG_QTYPE_Q5_1) {
-        uint32_t b = (p.hb >> (2 * (4 * s + r))) & 3u;
-        hq |= ((b & 1u) << 4) | ((b >> 1) << 20);
-      }
-      const __half2 d = (r & 1) ? dg8 : dg;
-      __half2 v;
-      if (QT == WG_QTYPE_Q4_0) v = __hmul2(__hsub2(u32_as_h2(hq), __float2half2_rn(1032.f)), d);
-      else if (QT == WG_QTYPE_Q5_0) v = __hmul2(__hsub2(u32_as_h2(hq), __float2half2_rn(1040.f)), d);
-      else {
-        const __half2 m = (r & 1) ? __high2half2(p.m) : __low2half2(p.m);
-        v = __hfma2(__hsub2(u32_as_h2(hq), __float2half2_rn(1024.f)), d, m);
-      }
-      a[r] = h2_as_u32(v);
-    }
-  }
-}
-
-__device__ __forceinline__ void epi_store(const Epi& e, int r, int n, float v) {
-  switch (e.mode) {
-    case EPI_F32:
-      if (e.bias) v = __fadd_rn(v, e.bias[n]);
-      e.out[(int64_t)r * e.ldo + n] = v;
-      break;
-    case EPI_RESID: {
-      float* p = e.out + (int64_t)r * e.ldo + n;
-      *p = __fadd_rn(*p, __fadd_rn(v, e.bias ? e.bias[n] : 0.f));
-      break;
-    }
-    case EPI_GELU_F16:
-      if (e.bias) v = __fadd_rn(v, e.bias[n]);
-      e.out16[(int64_t)r * e.ldo + n] = __float2half_rn(gelu_f32(v));
-      break;
-    case EPI_QKV: {
-      int seg = n / e.d, j = n - seg * e.d, h = j / e.hd, c = j - h * e.hd;
-      if (seg == 0) {
-        e.out[(int64_t)r * e.ldo + j] = __fadd_rn(v, e.bias_q[j]);
-      } else {
-        if (seg == 2) v = __fadd_rn(v, e.bias_v[j]);
-        int p = *e.pos;
-        e.kv[((((int64_t)r * 2 + (seg - 1)) * e.H + h) * e.T + p) * e.hd + c] = __float2half_rn(v);
-      }
-      break;
-    }
-    case EPI_CROSS_KV: {
-      int u = r / e.T, tt = r - u * e.T;
-      int lk = n / e.d, j = n - lk * e.d, l = lk >> 1, kv = lk & 1, h = j / e.hd, c = j - h * e.hd;
-      if (kv) v = __fadd_rn(v, e.bias_v[(int64_t)l * e.d + j]);
-      e.kv[(((((int64_t)l * e.U + u) * 2 + kv) * e.H + h) * e.T + tt) * e.hd + c] = __float2half_rn(v);
-      break;
-    }
-  }
-}
-
 
 // Output addressing of one weight row n: element (r, n) lives at
 // base + r * row_stride + col_off (CROSS_KV adds the utterance / frame split).
@@ -408,6 +277,16 @@ int launch_small_t(const DMat& W, const __half* X, int ldx, int R, const Epi& e,
                       "gemv_small");
 }
 
+// WG_GEMM_SMALL_PATH=4 keeps rows <= 16 on the streaming kernel (A/B comparisons).
+int small_path_override() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("WG_GEMM_SMALL_PATH");
+    v = (s && *s) ? atoi(s) : 0;
+  }
+  return v;
+}
+
 // WG_GEMM_LARGE_PATH=2 keeps rows > 16 on the mma.sync kernel (A/B comparisons).
 int large_path_override() {
   static int v = -1;
@@ -424,6 +303,8 @@ int launch_q(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaS
     path = R <= 16 ? 1 : (tc_supported(W) ? 3 : 2);
     if (path == 3 && large_path_override() == 2) path = 2;
   }
+  if (path == 1 && gemv_bulk_supported(W, R) && small_path_override() != 4) return launch_gemv_bulk(W, X, ldx, R, e, st);
+  if (path == 4) path = 1;
   if (path == 3) {
     if (!tc_supported(W)) {
       set_error("tcgen05 path needs a quantised matrix with K %% 64 == 0 (K=%d)", W.cols);

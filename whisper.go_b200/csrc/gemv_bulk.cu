@@ -1,0 +1,283 @@
+// gemv_bulk.cu — small-batch dequant GEMV (R <= 16 activation rows):
+// out[r, n] = sum_k X[r, k] * deq(W[n, k]), the decode-time form of
+// ml.MatMulQuantTransBInto (internal/ml/matmul_q8.go:93-119) at batch 1-3.
+//
+// Each CTA owns one 128-row weight group (8 tiles of 16 rows) and a range of
+// 64-wide K chunks. In the tile128 layout that slice of every plane (codes,
+// scales, mins, 5th bits) is one contiguous run, so the CTA fetches it into
+// shared memory with a few bulk copies, issued before the programmatic
+// dependency wait: weights are never written by the token loop, so their
+// HBM latency overlaps the previous kernel. After the wait the CTA stages its
+// K range of the activation rows, warp w multiplies tile w on mma.m16n8k16
+// (f16 A fragments dequantised from shared memory exactly as the streaming
+// kernels do, f32 accumulation), and the K ranges of a group — the CTAs of
+// one thread-block cluster — are summed in rank order through distributed
+// shared memory (deterministic), then stored through the Epi.
+#include <cooperative_groups.h>
+
+#include <algorithm>
+
+#include "async.cuh"
+#include "gemv_frag.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace wg {
+
+__device__ int g_gemv_error;  // first expired wait (code) of a gemv_bulk kernel
+
+namespace {
+
+constexpr int GB_WARPS = 8;          // one per 16-row tile of the group
+constexpr int GB_MAX_PAIRS = 12;     // 64-wide K chunks per CTA (shared memory bound)
+constexpr int GB_MAX_CLUSTER = 8;    // K ranges per group (portable cluster size)
+constexpr int GB_TARGET_CTAS = 296;  // two per SM
+
+struct GbLayout {
+  uint32_t qs, dsc, msc, hb, xs, red, bar, total;
+};
+
+// Shared-memory layout for np K chunks and RC activation rows.
+__host__ __device__ inline GbLayout gb_layout(uint32_t qt, int np, int RC) {
+  const uint32_t slots = (uint32_t)np * 16;
+  GbLayout L{};
+  L.qs = 0;
+  L.dsc = L.qs + slots * 32 * qtype_payload_bytes(qt);
+  L.msc = L.dsc + slots * 32;
+  L.hb = L.msc + (qtype_has_min(qt) ? slots * 32 : 0);
+  L.xs = L.hb + (qtype_has_hbits(qt) ? slots * 64 : 0);
+  const uint32_t xs_stride = (uint32_t)np * 64 + 16;  // halves; conflict-free 8-byte B-fragment loads
+  L.red = L.xs + ((uint32_t)RC * xs_stride * 2 + 15) / 16 * 16;
+  L.bar = L.red + 128u * RC * 4;
+  L.total = L.bar + 16;
+  return L;
+}
+
+template <uint32_t QT, int NB>
+__global__ void __launch_bounds__(GB_WARPS * 32)
+    gemv_bulk_kernel(DMat W, const __half* __restrict__ X, int ldx, int pairs_per, Epi e) {
+  constexpr int RC = NB * 8;
+  constexpr int pb = QT == WG_QTYPE_Q8_0 ? 16 : 8;
+  constexpr bool has_m = QT == WG_QTYPE_Q4_1 || QT == WG_QTYPE_Q5_1;
+  constexpr bool has_h = QT == WG_QTYPE_Q5_0 || QT == WG_QTYPE_Q5_1;
+  extern __shared__ __align__(128) unsigned char gb_smem[];
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int group = blockIdx.x;
+  const int kc = gridDim.z;
+  const int npairs_all = W.kblocks >> 1;
+  const int p0 = blockIdx.z * pairs_per;
+  const int np = min(pairs_per, npairs_all - p0);  // >= 1 (host choice)
+  const GbLayout L = gb_layout(QT, pairs_per, RC);
+  const uint32_t base = smem_u32(gb_smem);
+  const uint32_t bar = base + L.bar;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gb_smem + L.bar + 8);
+
+  // ---- weights: contiguous runs of the group's slots [S0, S0 + 16 np) ----
+  const int64_t S0 = ((int64_t)group * npairs_all + p0) * 16;
+  const uint32_t slots = (uint32_t)np * 16;
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_init(bar, 1);
+      *abort_flag = 0;
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      const uint32_t tx = slots * (32 * pb + 32 + (has_m ? 32 : 0) + (has_h ? 64 : 0));
+      mbar_arrive_tx(bar, tx);
+    }
+    __syncwarp();
+    // codes in up to 4 pieces (one per lane: a lane's copies complete in
+    // order, so separate lanes keep several in flight), then the scale planes
+    const uint32_t qbytes = slots * 32 * pb;
+    const uint32_t piece = (uint32_t)((np + 3) / 4) * 16 * 32 * pb;
+    if (lane < 4 && lane * piece < qbytes) {
+      const uint32_t off = lane * piece, n = min(piece, qbytes - off);
+      bulk_g2s(base + L.qs + off, W.qs + S0 * 32 * pb + off, n, bar);
+    }
+    if (lane == 4) bulk_g2s(base + L.dsc, W.dsc + S0 * 8, slots * 32, bar);
+    if (has_m && lane == 5) bulk_g2s(base + L.msc, W.msc + S0 * 8, slots * 32, bar);
+    if (has_h && lane == 6) bulk_g2s(base + L.hb, W.hb + S0 * 32, slots * 64, bar);
+  }
+
+  // ---- activations of this K range (written by earlier kernels) ----
+  pdl_wait();
+  const int k0 = p0 * 64, kn = np * 64;
+  const int xs_stride = pairs_per * 64 + 16;
+  __half* xsm = reinterpret_cast<__half*>(gb_smem + L.xs);
+  const int cpr = kn / 8;
+  for (int i = threadIdx.x; i < RC * cpr; i += blockDim.x) {
+    const int rr = i / cpr, cc = i - rr * cpr;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (rr < e.R) v = *reinterpret_cast<const uint4*>(X + (int64_t)rr * ldx + k0 + cc * 8);
+    *reinterpret_cast<uint4*>(xsm + rr * xs_stride + cc * 8) = v;
+  }
+  if (threadIdx.x == 0 && !mbar_wait(bar, 0, abort_flag, 1, &g_gemv_error)) mbar_drain(bar, 0);
+  __syncthreads();
+
+  // ---- warp w: tile w of the group over the CTA's K range ----
+  float acc[NB][4];
+#pragma unroll
+  for (int nb = 0; nb < NB; nb++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) acc[nb][c] = 0.f;
+  if (*abort_flag == 0) {
+    const unsigned char* qsm = gb_smem + L.qs;
+    const __half2* dsm = reinterpret_cast<const __half2*>(gb_smem + L.dsc);
+    const __half2* msm = reinterpret_cast<const __half2*>(gb_smem + L.msc);
+    const uint16_t* hsm = reinterpret_cast<const uint16_t*>(gb_smem + L.hb);
+    for (int kb = 0; kb < 2 * np; kb++) {
+      const int slot = (kb >> 1) * 16 + warp * 2 + (kb & 1);  // slot order inside a pair: tile, block
+      Pay p;
+      if (QT == WG_QTYPE_Q8_0) {
+        p.q = reinterpret_cast<const uint4*>(qsm)[slot * 32 + lane];
+      } else {
+        const uint2 v = reinterpret_cast<const uint2*>(qsm)[slot * 32 + lane];
+        p.q = make_uint4(v.x, v.y, 0, 0);
+      }
+      p.d = dsm[slot * 8 + g];
+      p.m = has_m ? msm[slot * 8 + g] : __float2half2_rn(0.f);
+      p.hb = has_h ? hsm[slot * 32 + lane] : 0u;
+#pragma unroll
+      for (int s = 0; s < 2; s++) {
+        uint32_t a[4];
+        dequant_step<QT>(p, s, a);
+        const int kk = kb * 32 + s * 16 + 4 * t;  // the payload's K order within 16 is the B fragment's
+#pragma unroll
+        for (int nb = 0; nb < NB; nb++) {
+          const uint2 bb = *reinterpret_cast<const uint2*>(xsm + (nb * 8 + g) * xs_stride + kk);
+          mma16816(acc[nb], a, bb.x, bb.y);
+        }
+      }
+    }
+  }
+  // partial tile [128 weight rows][RC activation rows]
+  float* red = reinterpret_cast<float*>(gb_smem + L.red);
+#pragma unroll
+  for (int nb = 0; nb < NB; nb++)
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+      red[(warp * 16 + g + 8 * (c >> 1)) * RC + nb * 8 + 2 * t + (c & 1)] = acc[nb][c];
+
+  // ---- sum the cluster's K ranges in rank order, store ----
+  cg::cluster_group cluster = cg::this_cluster();
+  if (kc > 1) cluster.sync();
+  else __syncthreads();
+  const int crank = kc > 1 ? (int)cluster.block_rank() : 0;
+  if (*abort_flag == 0) {
+    for (int o = crank * blockDim.x + threadIdx.x; o < 128 * RC; o += kc * blockDim.x) {
+      const int row = o / RC, col = o - row * RC;
+      const int n = group * 128 + row;
+      if (col >= e.R || n >= e.N) continue;
+      float v = 0.f;
+      if (kc > 1) {
+        float part[GB_MAX_CLUSTER];
+#pragma unroll
+        for (int k = 0; k < GB_MAX_CLUSTER; k++) part[k] = k < kc ? cluster.map_shared_rank(red, k)[o] : 0.f;
+#pragma unroll
+        for (int k = 0; k < GB_MAX_CLUSTER; k++)
+          if (k < kc) v += part[k];
+      } else {
+        v = red[o];
+      }
+      epi_store(e, col, n, v);
+    }
+  }
+  if (kc > 1) cluster.sync();  // peers may still read this CTA's partial tile
+}
+
+template <uint32_t QT, int NB>
+int launch_gb_t(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st) {
+  const int groups = (W.ntiles + 7) / 8, pairs = W.kblocks / 2;
+  int kc = std::min(GB_MAX_CLUSTER, std::max(1, (GB_TARGET_CTAS + groups - 1) / groups));
+  int per = (pairs + kc - 1) / kc;
+  if (per > GB_MAX_PAIRS) per = GB_MAX_PAIRS;
+  kc = (pairs + per - 1) / per;
+  if (kc > GB_MAX_CLUSTER) {
+    set_error("gemv_bulk: K=%d needs more than %d K ranges", W.cols, GB_MAX_CLUSTER);
+    return WG_ERR_UNSUPPORTED;
+  }
+  const GbLayout L = gb_layout(QT, per, NB * 8);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(groups, 1, kc);
+  cfg.blockDim = dim3(GB_WARPS * 32, 1, 1);
+  cfg.dynamicSmemBytes = L.total;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = kc;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  return launch_check(cudaLaunchKernelEx(&cfg, gemv_bulk_kernel<QT, NB>, W, X, ldx, per, e), "gemv_bulk");
+}
+
+template <uint32_t QT>
+int launch_gb_q(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st) {
+  return R <= 8 ? launch_gb_t<QT, 1>(W, X, ldx, R, e, st) : launch_gb_t<QT, 2>(W, X, ldx, R, e, st);
+}
+
+template <uint32_t QT, int NB>
+int configure_gb_t() {
+  cudaError_t e = cudaFuncSetAttribute(gemv_bulk_kernel<QT, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       227 * 1024);
+  if (e != cudaSuccess) {
+    set_error("cudaFuncSetAttribute(gemv_bulk): %s", cudaGetErrorString(e));
+    return WG_ERR_CUDA;
+  }
+  return WG_OK;
+}
+
+template <uint32_t QT>
+int configure_gb_q() {
+  int rc = configure_gb_t<QT, 1>();
+  return rc == WG_OK ? configure_gb_t<QT, 2>() : rc;
+}
+
+}  // namespace
+
+bool gemv_bulk_supported(const DMat& W, int R) {
+  return R >= 1 && R <= 16 && qtype_is_quant(W.qtype) && W.cols % 64 == 0 &&
+         (W.kblocks / 2 + GB_MAX_PAIRS - 1) / GB_MAX_PAIRS <= GB_MAX_CLUSTER;
+}
+
+int launch_gemv_bulk(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st) {
+  if (!gemv_bulk_supported(W, R)) {
+    set_error("gemv_bulk: unsupported shape (R=%d, K=%d, type %u)", R, W.cols, W.qtype);
+    return WG_ERR_UNSUPPORTED;
+  }
+  switch (W.qtype) {
+    case WG_QTYPE_Q8_0: return launch_gb_q<WG_QTYPE_Q8_0>(W, X, ldx, R, e, st);
+    case WG_QTYPE_Q4_0: return launch_gb_q<WG_QTYPE_Q4_0>(W, X, ldx, R, e, st);
+    case WG_QTYPE_Q4_1: return launch_gb_q<WG_QTYPE_Q4_1>(W, X, ldx, R, e, st);
+    case WG_QTYPE_Q5_0: return launch_gb_q<WG_QTYPE_Q5_0>(W, X, ldx, R, e, st);
+    default: return launch_gb_q<WG_QTYPE_Q5_1>(W, X, ldx, R, e, st);
+  }
+}
+
+int init_gemv_bulk_attributes() {
+  int rc = configure_gb_q<WG_QTYPE_Q8_0>();
+  if (rc == WG_OK) rc = configure_gb_q<WG_QTYPE_Q4_0>();
+  if (rc == WG_OK) rc = configure_gb_q<WG_QTYPE_Q4_1>();
+  if (rc == WG_OK) rc = configure_gb_q<WG_QTYPE_Q5_0>();
+  if (rc == WG_OK) rc = configure_gb_q<WG_QTYPE_Q5_1>();
+  return rc;
+}
+
+int gemv_error_word(int* word, bool clear) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_gemv_error, sizeof(int));
+  if (e != cudaSuccess) {
+    set_error("reading the gemv error word: %s", cudaGetErrorString(e));
+    return WG_ERR_CUDA;
+  }
+  if (clear && v) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_gemv_error, &z, sizeof(int));
+  }
+  *word = v;
+  return WG_OK;
+}
+
+}  // namespace wg

@@ -46,8 +46,10 @@ struct Epi {
 // with a 128 x 256 fp32 partial tile (19.4 MB).
 constexpr int64_t TC_SPLIT_WS_FLOATS = 148LL * 256 * 128;
 
-// path: 0 auto, 1 small-R kernel (mma.sync GEMV), 2 large-R mma.sync kernel,
-// 3 tcgen05 tensor-core kernel (quantised weights, K % 64 == 0).
+// path: 0 auto, 1 small-R kernel (R <= 16: the bulk-copy GEMV where it
+// applies, else the streaming one), 2 large-R mma.sync kernel, 3 tcgen05
+// tensor-core kernel (quantised weights, K % 64 == 0), 4 streaming small-R
+// kernel.
 int init_gemm_attributes();
 int init_tc_attributes();
 bool tc_supported(const DMat& W);
@@ -56,6 +58,12 @@ int launch_matmul_tc(const DMat& W, const __half* X, int ldx, int R, const Epi& 
 int tc_error_word(int* word, bool clear);
 int launch_matmul(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st,
                   int path = 0);
+// small-batch GEMV with bulk-copied weight slices (gemv_bulk.cu), R <= 16
+bool gemv_bulk_supported(const DMat& W, int R);
+int launch_gemv_bulk(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st);
+int init_gemv_bulk_attributes();
+// First expired bounded wait of a gemv_bulk kernel on the current device (0: none).
+int gemv_error_word(int* word, bool clear);
 
 // ---- elementwise (eltwise.cu) -----------------------------------------------------
 // x[r] = dequant(tok_emb row tok[r]) + pos_emb[pos]   (decoder.go:756-773, Q1 fix)
