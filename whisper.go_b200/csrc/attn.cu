@@ -247,7 +247,6 @@ __global__ void __launch_bounds__(XA_MAX_WARPS * 32)
     cross_attn_mma_kernel(const float* __restrict__ q, const __half* __restrict__ kvc, int U, int B, int H, int T,
                           int wpc, __half* __restrict__ out16, int ldo) {
   pdl_trigger();
-  pdl_wait();
   extern __shared__ __align__(128) unsigned char smem[];
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
@@ -283,6 +282,10 @@ __global__ void __launch_bounds__(XA_MAX_WARPS * 32)
     cp_async16(vs_addr + row * 128 + ((ch ^ (row & 7)) << 4), vbase + (int64_t)tt * 64 + ch * 8, ok);
   }
   asm volatile("cp.async.commit_group;\n" ::);
+  // the cross K/V cache is written once per decode, before the token loop
+  // (its precompute is followed by a fully serialised launch), so its loads
+  // above overlap the previous kernel; q is written by it
+  pdl_wait();
   // Q fragments (rows = beams of utterance u), scaled by 1/sqrt(64) = 2^-3 (exact)
   uint32_t qa[4][4];
   {
@@ -468,7 +471,6 @@ __global__ void __launch_bounds__(XS_THREADS, 2)
     cross_attn_stream_kernel(const float* __restrict__ q, const __grid_constant__ CUtensorMap kvmap, int B, int H,
                              int T, __half* __restrict__ out16, int ldo) {
   pdl_trigger();
-  pdl_wait();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int h = blockIdx.x, u = blockIdx.y;
@@ -513,6 +515,10 @@ __global__ void __launch_bounds__(XS_THREADS, 2)
     return;
   }
   // ---------------- consumers ----------------
+  // The producer streams the cross K/V cache, written once per decode before
+  // the token loop (its precompute is followed by a fully serialised launch),
+  // without waiting for the previous kernel; q is written by it.
+  pdl_wait();
   // Q A-fragments (rows 0-7 = beams; rows 8-15 are zero), scaled by 2^-3
   uint32_t qa[4][2];
   {

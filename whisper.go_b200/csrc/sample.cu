@@ -471,8 +471,13 @@ int launch_pos_inc(const SampleState& s, cudaStream_t st) {
   return launch_check(launch_k(pos_inc_kernel, dim3(1), dim3(1), 0, st, s.pos, (int*)nullptr), "pos_inc");
 }
 
+// Launched without programmatic serialisation: it starts only once every
+// earlier kernel of the stream (the cross K/V precompute) has completed, and
+// no later kernel can start before it, so the token loop's kernels may read
+// the cross K/V cache before their dependency wait.
 int launch_sample_reset(const SampleState& s, const int* prompt_dev, cudaStream_t st) {
-  return launch_check(launch_k(reset_kernel, dim3(s.R), dim3(128), 0, st, s, prompt_dev), "sample_reset");
+  reset_kernel<<<s.R, 128, 0, st>>>(s, prompt_dev);
+  return launch_status("sample_reset");
 }
 
 }  // namespace wg
