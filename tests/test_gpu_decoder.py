@@ -167,3 +167,33 @@ def test_teacher_forced_tensor_core_path(qtype):
     finally:
         dec.close()
         m.close()
+
+
+_LN_FUSE_SCRIPT = r"""
+import sys, numpy as np
+sys.path[:0] = [{pkg!r}]
+import wgdec
+m = wgdec.SyntheticModel(51864, {d}, {d} // 64, 2, 448, "Q8_0", seed=31)
+dec = wgdec.WhisperDecoder(m)
+encs = [m.encoder_output(u, 96) for u in range(2)]
+forced = np.random.default_rng(3).integers(0, 50257, size=(2, 3))
+np.save({out!r}, dec.teacher_forced_logits(encs, [50258, 50259, 50357, 50363], forced, wgdec.MODE_CORRECT))
+"""
+
+
+@pytest.mark.parametrize("d", [256, 384])
+def test_fused_input_layernorm_is_bit_identical(tmp_path, d):
+    """The small-batch GEMV's own LayerNorm (WG_LN_FUSE=1, the default) gives
+    exactly the logits of the separate LayerNorm kernel (WG_LN_FUSE=0), for
+    the lane-strided (d = 256) and float4 (d = 384) summation orders."""
+    import os
+    import subprocess
+    import sys
+    outs = []
+    for fuse in ("0", "1"):
+        out = tmp_path / ("logits_%s.npy" % fuse)
+        code = _LN_FUSE_SCRIPT.format(pkg=str(wgdec.PKG), d=d, out=str(out))
+        env = dict(os.environ, WG_LN_FUSE=fuse)
+        subprocess.run([sys.executable, "-c", code], env=env, check=True, timeout=300)
+        outs.append(np.load(out))
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))

@@ -279,12 +279,24 @@ int forward_step(wg_model* m, DevJob& j, const int* tokens, bool want_logits, in
   const int64_t layer_kv = (int64_t)R * 2 * H * j.Tmax * hd;
   const int64_t layer_cross = (int64_t)j.U * 2 * H * j.T * hd;
   const bool ref = mode == WG_MODE_REF_COMPAT;
+  // LayerNorm of x feeding matmul W: left to the small-batch GEMV where it
+  // can take it (no separate kernel), else a LayerNorm kernel into xln16
+  auto norm_for = [&](const DMat& W, const float* w, const float* b, Epi& e) -> int {
+    if (matmul_fuses_input_ln(W, R)) {
+      e.ln_x = j.x;
+      e.ln_w = w;
+      e.ln_b = b;
+      e.ln_d = d;
+      return WG_OK;
+    }
+    return launch_layernorm(j.x, w, b, R, d, j.xln16, nullptr, st);
+  };
   for (int l = 0; l < m->L; l++) {
     const DevLayer& ly = dm.layers[l];
     __half* kv = j.selfkv + l * layer_kv;
     // self-attention (decoder.go:836-908)
-    WG_CHECK(launch_layernorm(j.x, ly.sln_w, ly.sln_b, R, d, j.xln16, nullptr, st));
     Epi e = job_epi(j);
+    WG_CHECK(norm_for(ly.qkv, ly.sln_w, ly.sln_b, e));
     e.mode = EPI_QKV; e.out = j.q; e.ldo = d; e.d = d; e.H = H; e.hd = hd; e.T = j.Tmax; e.pos = j.ss.pos;
     e.kv = kv; e.bias_q = ly.q_b; e.bias_v = ly.v_b; e.N = 3 * d;
     WG_CHECK(launch_matmul(ly.qkv, j.xln16, j.ldd, R, e, st));
@@ -296,8 +308,9 @@ int forward_step(wg_model* m, DevJob& j, const int* tokens, bool want_logits, in
     e = job_epi(j); e.mode = EPI_RESID; e.out = j.x; e.ldo = d; e.bias = ly.so_b; e.N = d;
     WG_CHECK(launch_matmul(ly.so, j.attn16, j.ldd, R, e, st));
     // cross-attention (decoder.go:911-971)
-    WG_CHECK(launch_layernorm(j.x, ly.cln_w, ly.cln_b, R, d, j.xln16, nullptr, st));
-    e = job_epi(j); e.mode = EPI_F32; e.out = j.q; e.ldo = d; e.bias = ly.cq_b; e.N = d;
+    e = job_epi(j);
+    WG_CHECK(norm_for(ly.cq, ly.cln_w, ly.cln_b, e));
+    e.mode = EPI_F32; e.out = j.q; e.ldo = d; e.bias = ly.cq_b; e.N = d;
     WG_CHECK(launch_matmul(ly.cq, j.xln16, j.ldd, R, e, st));
     CrossAttnArgs ca{};
     ca.q = j.q; ca.kv = j.cross + l * layer_cross; ca.U = j.U; ca.B = j.B; ca.H = H; ca.hd = hd; ca.T = j.T;
@@ -306,15 +319,16 @@ int forward_step(wg_model* m, DevJob& j, const int* tokens, bool want_logits, in
     e = job_epi(j); e.mode = EPI_RESID; e.out = j.x; e.ldo = d; e.bias = ly.co_b; e.N = d;
     WG_CHECK(launch_matmul(ly.co, j.attn16, j.ldd, R, e, st));
     // MLP (decoder.go:974-993)
-    WG_CHECK(launch_layernorm(j.x, ly.mln_w, ly.mln_b, R, d, j.xln16, nullptr, st));
-    e = job_epi(j); e.mode = EPI_GELU_F16; e.out16 = j.h16; e.ldo = j.ld4; e.bias = ly.m0_b; e.N = 4 * d;
+    e = job_epi(j);
+    WG_CHECK(norm_for(ly.m0, ly.mln_w, ly.mln_b, e));
+    e.mode = EPI_GELU_F16; e.out16 = j.h16; e.ldo = j.ld4; e.bias = ly.m0_b; e.N = 4 * d;
     WG_CHECK(launch_matmul(ly.m0, j.xln16, j.ldd, R, e, st));
     e = job_epi(j); e.mode = EPI_RESID; e.out = j.x; e.ldo = d; e.bias = ly.m2_b; e.N = d;
     WG_CHECK(launch_matmul(ly.m2, j.h16, j.ld4, R, e, st));
   }
   if (!want_logits) return WG_OK;
-  WG_CHECK(launch_layernorm(j.x, dm.ln_w, dm.ln_b, R, d, j.xln16, nullptr, st));  // decoder.go:818
   Epi e = job_epi(j);
+  WG_CHECK(norm_for(dm.tok, dm.ln_w, dm.ln_b, e));  // decoder.go:818
   e.mode = EPI_F32; e.out = j.logits; e.ldo = m->V; e.N = m->V;
   return launch_matmul(dm.tok, j.xln16, j.ldd, R, e, st);  // decoder.go:823 (tied embedding)
 }

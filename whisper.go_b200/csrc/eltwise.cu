@@ -146,6 +146,8 @@ int launch_embed(const DMat& te, const float* pos_emb, const int* tokens, const 
                       "embed");
 }
 
+bool layernorm_uses_vec(int d) { return d == 384 || d == 512 || d == 768 || d == 1024 || d == 1280; }
+
 int launch_layernorm(const float* x, const float* w, const float* b, int R, int d, __half* out16, float* out32,
                      cudaStream_t st) {
   int ld16 = (d + 7) / 8 * 8;

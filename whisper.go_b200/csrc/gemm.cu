@@ -305,6 +305,10 @@ int launch_q(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaS
   }
   if (path == 1 && gemv_bulk_supported(W, R) && small_path_override() != 4) return launch_gemv_bulk(W, X, ldx, R, e, st);
   if (path == 4) path = 1;
+  if (e.ln_x) {
+    set_error("launch_matmul: a fused input LayerNorm needs the small-batch GEMV");
+    return WG_ERR_INVALID;
+  }
   if (path == 3) {
     if (!tc_supported(W)) {
       set_error("tcgen05 path needs a quantised matrix with K %% 64 == 0 (K=%d)", W.cols);
@@ -338,6 +342,15 @@ int init_gemm_attributes() {
   WG_CFG(WG_QTYPE_Q5_1)
 #undef WG_CFG
   return rc;
+}
+
+bool matmul_fuses_input_ln(const DMat& W, int R) {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("WG_LN_FUSE");
+    v = (s && *s) ? atoi(s) : 1;
+  }
+  return v != 0 && R <= 16 && gemv_bulk_supported(W, R) && small_path_override() != 4;
 }
 
 int launch_matmul(const DMat& W, const __half* X, int ldx, int R, const Epi& e_in, cudaStream_t st, int path) {

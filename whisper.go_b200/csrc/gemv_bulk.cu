@@ -34,7 +34,7 @@ constexpr int GB_MAX_CLUSTER = 8;    // K ranges per group (portable cluster siz
 constexpr int GB_TARGET_CTAS = 296;  // two per SM
 
 struct GbLayout {
-  uint32_t qs, dsc, msc, hb, xs, red, bar, total;
+  uint32_t qs, dsc, msc, hb, xs, red, stat, bar, total;
 };
 
 // Shared-memory layout for np K chunks and RC activation rows.
@@ -48,14 +48,52 @@ __host__ __device__ inline GbLayout gb_layout(uint32_t qt, int np, int RC) {
   L.xs = L.hb + (qtype_has_hbits(qt) ? slots * 64 : 0);
   const uint32_t xs_stride = (uint32_t)np * 64 + 16;  // halves; conflict-free 8-byte B-fragment loads
   L.red = L.xs + ((uint32_t)RC * xs_stride * 2 + 15) / 16 * 16;
-  L.bar = L.red + 128u * RC * 4;
+  L.stat = L.red + 128u * RC * 4;  // [RC][2] LayerNorm mean, std
+  L.bar = L.stat + (uint32_t)RC * 8;
   L.total = L.bar + 16;
   return L;
 }
 
+// Mean and standard deviation of one row of d floats by one warp, with the
+// arithmetic of the LayerNorm kernels (internal/ml/ops.go:153-202): vec —
+// per-lane float4 runs lane + 32 i (layernorm_reg_kernel), else lane-strided
+// scalars (layernorm_kernel); warp tree sums; two passes; sqrt(var + 1e-5).
+__device__ __forceinline__ void ln_row_stats(const float* __restrict__ xr, int d, bool vec, int lane, float& mean,
+                                             float& sd) {
+  float s = 0.f, q = 0.f;
+  if (vec) {
+    const float4* x4 = reinterpret_cast<const float4*>(xr);
+    for (int i = lane; i < d / 4; i += 32) {
+      const float4 v = x4[i];
+      s += (v.x + v.y) + (v.z + v.w);
+    }
+    s = warp_sum(s);
+    mean = __fdiv_rn(s, (float)d);
+    for (int i = lane; i < d / 4; i += 32) {
+      const float4 v = x4[i];
+      const float a = __fsub_rn(v.x, mean), b = __fsub_rn(v.y, mean), c = __fsub_rn(v.z, mean),
+                  e = __fsub_rn(v.w, mean);
+      q = __fmaf_rn(a, a, q);
+      q = __fmaf_rn(b, b, q);
+      q = __fmaf_rn(c, c, q);
+      q = __fmaf_rn(e, e, q);
+    }
+  } else {
+    for (int i = lane; i < d; i += 32) s += xr[i];
+    s = warp_sum(s);
+    mean = __fdiv_rn(s, (float)d);
+    for (int i = lane; i < d; i += 32) {
+      const float dd = __fsub_rn(xr[i], mean);
+      q = __fmaf_rn(dd, dd, q);
+    }
+  }
+  q = warp_sum(q);
+  sd = __fsqrt_rn(__fadd_rn(__fdiv_rn(q, (float)d), 1e-5f));
+}
+
 template <uint32_t QT, int NB>
 __global__ void __launch_bounds__(GB_WARPS * 32)
-    gemv_bulk_kernel(DMat W, const __half* __restrict__ X, int ldx, int pairs_per, Epi e) {
+    gemv_bulk_kernel(DMat W, const __half* __restrict__ X, int ldx, int pairs_per, int ln_vec, Epi e) {
   constexpr int RC = NB * 8;
   constexpr int pb = QT == WG_QTYPE_Q8_0 ? 16 : 8;
   constexpr bool has_m = QT == WG_QTYPE_Q4_1 || QT == WG_QTYPE_Q5_1;
@@ -103,12 +141,36 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
   const int k0 = p0 * 64, kn = np * 64;
   const int xs_stride = pairs_per * 64 + 16;
   __half* xsm = reinterpret_cast<__half*>(gb_smem + L.xs);
-  const int cpr = kn / 8;
-  for (int i = threadIdx.x; i < RC * cpr; i += blockDim.x) {
-    const int rr = i / cpr, cc = i - rr * cpr;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (rr < e.R) v = *reinterpret_cast<const uint4*>(X + (int64_t)rr * ldx + k0 + cc * 8);
-    *reinterpret_cast<uint4*>(xsm + rr * xs_stride + cc * 8) = v;
+  if (e.ln_x) {
+    // fused LayerNorm: every CTA takes the statistics of the (<= 16) rows
+    // and normalises its own K range, element by element as the kernel does
+    float* stat = reinterpret_cast<float*>(gb_smem + L.stat);
+    for (int rr = warp; rr < e.R; rr += GB_WARPS) {
+      float mean, sd;
+      ln_row_stats(e.ln_x + (int64_t)rr * e.ln_d, e.ln_d, ln_vec != 0, lane, mean, sd);
+      if (lane == 0) {
+        stat[2 * rr] = mean;
+        stat[2 * rr + 1] = sd;
+      }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < RC * kn; i += blockDim.x) {
+      const int rr = i / kn, kk = i - rr * kn, k = k0 + kk;
+      float o = 0.f;
+      if (rr < e.R) {
+        const float x = e.ln_x[(int64_t)rr * e.ln_d + k];
+        o = __fadd_rn(__fdiv_rn(__fmul_rn(e.ln_w[k], __fsub_rn(x, stat[2 * rr])), stat[2 * rr + 1]), e.ln_b[k]);
+      }
+      xsm[rr * xs_stride + kk] = __float2half_rn(o);
+    }
+  } else {
+    const int cpr = kn / 8;
+    for (int i = threadIdx.x; i < RC * cpr; i += blockDim.x) {
+      const int rr = i / cpr, cc = i - rr * cpr;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (rr < e.R) v = *reinterpret_cast<const uint4*>(X + (int64_t)rr * ldx + k0 + cc * 8);
+      *reinterpret_cast<uint4*>(xsm + rr * xs_stride + cc * 8) = v;
+    }
   }
   if (threadIdx.x == 0 && !mbar_wait(bar, 0, abort_flag, 1, &g_gemv_error)) mbar_drain(bar, 0);
   __syncthreads();
@@ -210,7 +272,8 @@ int launch_gb_t(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cu
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  return launch_check(cudaLaunchKernelEx(&cfg, gemv_bulk_kernel<QT, NB>, W, X, ldx, per, e), "gemv_bulk");
+  const int ln_vec = e.ln_x && layernorm_uses_vec(e.ln_d) ? 1 : 0;
+  return launch_check(cudaLaunchKernelEx(&cfg, gemv_bulk_kernel<QT, NB>, W, X, ldx, per, ln_vec, e), "gemv_bulk");
 }
 
 template <uint32_t QT>

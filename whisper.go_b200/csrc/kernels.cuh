@@ -40,6 +40,13 @@ struct Epi {
   // (no other launch may use it concurrently); contents need no initialisation
   float* split_ws = nullptr;
   int64_t split_ws_floats = 0;
+  // Small-batch path only (matmul_fuses_input_ln): the activations are
+  // LayerNorm(ln_x) of ln_d-wide fp32 rows, normalised inside the GEMV with
+  // the LayerNorm kernel's arithmetic (X is not read).
+  const float* ln_x = nullptr;
+  const float* ln_w = nullptr;
+  const float* ln_b = nullptr;
+  int ln_d = 0;
 };
 
 // Upper bound of the split-K workspace: at most one wave of 148 CTAs, each
@@ -58,6 +65,9 @@ int launch_matmul_tc(const DMat& W, const __half* X, int ldx, int R, const Epi& 
 int tc_error_word(int* word, bool clear);
 int launch_matmul(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st,
                   int path = 0);
+// True when launch_matmul(path 0) of W x [R rows] honours Epi.ln_x, i.e. the
+// LayerNorm before the matmul can be left to the GEMV (WG_LN_FUSE=0: never).
+bool matmul_fuses_input_ln(const DMat& W, int R);
 // small-batch GEMV with bulk-copied weight slices (gemv_bulk.cu), R <= 16
 bool gemv_bulk_supported(const DMat& W, int R);
 int launch_gemv_bulk(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st);
@@ -72,6 +82,9 @@ int launch_embed(const DMat& tok_emb, const float* pos_emb, const int* tokens, c
 // out16[r] = half(LayerNorm(x[r]))  (ml/ops.go:153-202); optional fp32 copy
 int launch_layernorm(const float* x, const float* w, const float* b, int R, int d, __half* out16,
                      float* out32, cudaStream_t st);
+// True when launch_layernorm sums a row as per-lane float4 runs (the register
+// kernel) rather than lane-strided scalars.
+bool layernorm_uses_vec(int d);
 int launch_f32_to_f16(const float* in, __half* out, int64_t n, cudaStream_t st);
 
 // ---- attention (attn.cu) ------------------------------------------------------------
