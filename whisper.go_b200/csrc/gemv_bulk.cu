@@ -54,6 +54,8 @@ __host__ __device__ inline GbLayout gb_layout(uint32_t qt, int np, int RC) {
   return L;
 }
 
+constexpr int LN_MAX_NV = 10;  // float4 runs per lane of the vec layout (d <= 1280)
+
 // Mean and standard deviation of one row of d floats by one warp, with the
 // arithmetic of the LayerNorm kernels (internal/ml/ops.go:153-202): vec —
 // per-lane float4 runs lane + 32 i (layernorm_reg_kernel), else lane-strided
@@ -61,22 +63,28 @@ __host__ __device__ inline GbLayout gb_layout(uint32_t qt, int np, int RC) {
 __device__ __forceinline__ void ln_row_stats(const float* __restrict__ xr, int d, bool vec, int lane, float& mean,
                                              float& sd) {
   float s = 0.f, q = 0.f;
-  if (vec) {
+  if (vec) {  // d = 128 nv, nv <= LN_MAX_NV: the row in registers, all loads in flight at once
     const float4* x4 = reinterpret_cast<const float4*>(xr);
-    for (int i = lane; i < d / 4; i += 32) {
-      const float4 v = x4[i];
-      s += (v.x + v.y) + (v.z + v.w);
-    }
+    const int nv = d >> 7;
+    float4 v[LN_MAX_NV];
+#pragma unroll
+    for (int j = 0; j < LN_MAX_NV; j++)
+      if (j < nv) v[j] = x4[lane + 32 * j];
+#pragma unroll
+    for (int j = 0; j < LN_MAX_NV; j++)
+      if (j < nv) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
     s = warp_sum(s);
     mean = __fdiv_rn(s, (float)d);
-    for (int i = lane; i < d / 4; i += 32) {
-      const float4 v = x4[i];
-      const float a = __fsub_rn(v.x, mean), b = __fsub_rn(v.y, mean), c = __fsub_rn(v.z, mean),
-                  e = __fsub_rn(v.w, mean);
-      q = __fmaf_rn(a, a, q);
-      q = __fmaf_rn(b, b, q);
-      q = __fmaf_rn(c, c, q);
-      q = __fmaf_rn(e, e, q);
+#pragma unroll
+    for (int j = 0; j < LN_MAX_NV; j++) {
+      if (j < nv) {
+        const float a = __fsub_rn(v[j].x, mean), b = __fsub_rn(v[j].y, mean), c = __fsub_rn(v[j].z, mean),
+                    e = __fsub_rn(v[j].w, mean);
+        q = __fmaf_rn(a, a, q);
+        q = __fmaf_rn(b, b, q);
+        q = __fmaf_rn(c, c, q);
+        q = __fmaf_rn(e, e, q);
+      }
     }
   } else {
     for (int i = lane; i < d; i += 32) s += xr[i];
@@ -154,14 +162,23 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
       }
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < RC * kn; i += blockDim.x) {
-      const int rr = i / kn, kk = i - rr * kn, k = k0 + kk;
-      float o = 0.f;
+    // four adjacent elements per thread (d and the K range are multiples of 64)
+    const int kq = kn / 4;
+    for (int i = threadIdx.x; i < RC * kq; i += blockDim.x) {
+      const int rr = i / kq, kk = 4 * (i - rr * kq), k = k0 + kk;
+      float o[4] = {0.f, 0.f, 0.f, 0.f};
       if (rr < e.R) {
-        const float x = e.ln_x[(int64_t)rr * e.ln_d + k];
-        o = __fadd_rn(__fdiv_rn(__fmul_rn(e.ln_w[k], __fsub_rn(x, stat[2 * rr])), stat[2 * rr + 1]), e.ln_b[k]);
+        const float4 x = *reinterpret_cast<const float4*>(e.ln_x + (int64_t)rr * e.ln_d + k);
+        const float4 w = *reinterpret_cast<const float4*>(e.ln_w + k);
+        const float4 b = *reinterpret_cast<const float4*>(e.ln_b + k);
+        const float mean = stat[2 * rr], sd = stat[2 * rr + 1];
+        o[0] = __fadd_rn(__fdiv_rn(__fmul_rn(w.x, __fsub_rn(x.x, mean)), sd), b.x);
+        o[1] = __fadd_rn(__fdiv_rn(__fmul_rn(w.y, __fsub_rn(x.y, mean)), sd), b.y);
+        o[2] = __fadd_rn(__fdiv_rn(__fmul_rn(w.z, __fsub_rn(x.z, mean)), sd), b.z);
+        o[3] = __fadd_rn(__fdiv_rn(__fmul_rn(w.w, __fsub_rn(x.w, mean)), sd), b.w);
       }
-      xsm[rr * xs_stride + kk] = __float2half_rn(o);
+      const __half2 h0 = __floats2half2_rn(o[0], o[1]), h1 = __floats2half2_rn(o[2], o[3]);
+      *reinterpret_cast<uint2*>(xsm + rr * xs_stride + kk) = make_uint2(h2_as_u32(h0), h2_as_u32(h1));
     }
   } else {
     const int cpr = kn / 8;
