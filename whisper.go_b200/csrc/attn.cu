@@ -731,7 +731,10 @@ int launch_cross_attn(const CrossAttnArgs& c, cudaStream_t st) {
   }
   const bool stream_ok = c.B <= 8 && c.T <= XS_MAXCH * XS_CH;
   const int ov = xattn_override();
-  if (stream_ok && (ov == 2 || (ov == 0 && c.U * c.H >= 2 * 148))) {
+  // streaming (one CTA per head and utterance) from U * H >= 64 on: measured
+  // faster at U * H = 128 (medium, 8 utterances: 16.4 vs ~37 us per launch),
+  // 160 and 1280; below, the cluster kernel's 8-way frame split wins
+  if (stream_ok && (ov == 2 || (ov == 0 && c.U * c.H >= 64))) {
     // the layer's cache as [U*2*H slabs][T frames][64] f16, box [1][XS_CH][64]
     EncodeTiledFn enc = encode_fn();
     if (!enc) {
