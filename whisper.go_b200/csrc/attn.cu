@@ -48,10 +48,17 @@ struct SimtArgs {
   int ldo;
 };
 
-constexpr int SIMT_WARPS = 4;
+constexpr int SIMT_WARPS = 16;  // most warps per CTA (launch picks 4 or 16)
 constexpr int SIMT_UNROLL = 4;  // warp steps whose loads are issued together
 
-__global__ void __launch_bounds__(SIMT_WARPS * 32) attn_simt_kernel(SimtArgs a) {
+// NW warps share the positions, 4 per warp step. NW = 16 (few CTAs in
+// flight, latency-bound): when one round of loads covers all n positions
+// (n <= 256) each lane's V rows are loaded together with its K rows and kept
+// in registers through the softmax, one dependent round of loads instead of
+// four. NW = 4 (large batches, where the HBM stream is the limit): K pass,
+// then V pass, at the register count that keeps occupancy up.
+template <int NW>
+__global__ void __launch_bounds__(NW * 32) attn_simt_kernel(SimtArgs a) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ float sm[];  // scores [n] then reduction scratch
@@ -80,7 +87,10 @@ __global__ void __launch_bounds__(SIMT_WARPS * 32) attn_simt_kernel(SimtArgs a) 
   };
   // scores: each warp step covers 4 positions (8 lanes x 8 dims each); the
   // table lookups and K rows of SIMT_UNROLL steps are loaded before use
-  const int step = SIMT_WARPS * 4;
+  constexpr int nw = NW;
+  const int step = nw * 4;
+  const bool one_round = NW == SIMT_WARPS && n <= step * SIMT_UNROLL && hd == 64;
+  uint4 vkeep[SIMT_UNROLL];  // one_round: this lane's V rows, loaded with the K rows
   for (int tb = warp * 4; tb < n; tb += step * SIMT_UNROLL) {
     int64_t off[SIMT_UNROLL];
 #pragma unroll
@@ -93,6 +103,12 @@ __global__ void __launch_bounds__(SIMT_WARPS * 32) attn_simt_kernel(SimtArgs a) 
 #pragma unroll
       for (int u = 0; u < SIMT_UNROLL; u++)
         kraw[u] = off[u] >= 0 ? *reinterpret_cast<const uint4*>(a.kv + off[u] + dl) : make_uint4(0, 0, 0, 0);
+      if (one_round) {
+#pragma unroll
+        for (int u = 0; u < SIMT_UNROLL; u++)
+          vkeep[u] = off[u] >= 0 ? *reinterpret_cast<const uint4*>(a.kv + off[u] + a.v_off + dl)
+                                 : make_uint4(0, 0, 0, 0);
+      }
     }
 #pragma unroll
     for (int u = 0; u < SIMT_UNROLL; u++) {
@@ -129,7 +145,7 @@ __global__ void __launch_bounds__(SIMT_WARPS * 32) attn_simt_kernel(SimtArgs a) 
   if (lane == 0) red[warp] = m;
   __syncthreads();
   m = red[0];
-  for (int w = 1; w < SIMT_WARPS; w++) m = fmaxf(m, red[w]);
+  for (int w = 1; w < nw; w++) m = fmaxf(m, red[w]);
   __syncthreads();
   // exp + sum
   float s = 0.f;
@@ -142,7 +158,7 @@ __global__ void __launch_bounds__(SIMT_WARPS * 32) attn_simt_kernel(SimtArgs a) 
   if (lane == 0) red[warp] = s;
   __syncthreads();
   s = 0.f;
-  for (int w = 0; w < SIMT_WARPS; w++) s += red[w];
+  for (int w = 0; w < nw; w++) s += red[w];
   const float inv = s == 0.f ? 0.f : __fdiv_rn(1.0f, s);
   const float uni = __fdiv_rn(1.0f, (float)n);
   for (int t = threadIdx.x; t < n; t += blockDim.x) scores[t] = s == 0.f ? uni : __fmul_rn(scores[t], inv);
@@ -151,7 +167,23 @@ __global__ void __launch_bounds__(SIMT_WARPS * 32) attn_simt_kernel(SimtArgs a) 
   float o[8];
 #pragma unroll
   for (int e = 0; e < 8; e++) o[e] = 0.f;
-  for (int tb = warp * 4; tb < n; tb += step * SIMT_UNROLL) {
+  if (one_round) {
+    const int tb = warp * 4;
+#pragma unroll
+    for (int u = 0; u < SIMT_UNROLL; u++) {
+      const int t = tb + u * step + sub;
+      if (t >= n) continue;
+      const float w = scores[t];
+      const __half2* v2 = reinterpret_cast<const __half2*>(&vkeep[u]);
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        float2 vf = __half22float2(v2[e]);
+        o[2 * e] = fmaf(w, vf.x, o[2 * e]);
+        o[2 * e + 1] = fmaf(w, vf.y, o[2 * e + 1]);
+      }
+    }
+  }
+  for (int tb = warp * 4; !one_round && tb < n; tb += step * SIMT_UNROLL) {
     int64_t off[SIMT_UNROLL];
 #pragma unroll
     for (int u = 0; u < SIMT_UNROLL; u++) {
@@ -195,7 +227,7 @@ __global__ void __launch_bounds__(SIMT_WARPS * 32) attn_simt_kernel(SimtArgs a) 
   __syncthreads();
   for (int c = threadIdx.x; c < hd; c += blockDim.x) {
     float v = ored[c];
-    for (int w = 1; w < SIMT_WARPS; w++) v += ored[w * 64 + c];
+    for (int w = 1; w < nw; w++) v += ored[w * 64 + c];
     out[c] = __float2half_rn(v);
   }
 }
@@ -206,7 +238,16 @@ int launch_simt(const SimtArgs& a, int R, int n_max, cudaStream_t st) {
     set_error("attention: %d positions exceed the SIMT kernel's shared memory", n_max);
     return WG_ERR_UNSUPPORTED;
   }
-  return launch_check(launch_k(attn_simt_kernel, dim3(R, a.H), dim3(SIMT_WARPS * 32), smem, st, a), "attn_simt");
+  // 16 warps while few CTAs are in flight (latency-bound), 4 beyond
+  static int many = -1;
+  if (many < 0) {
+    const char* s = getenv("WG_SELF_MANY");
+    many = (s && *s) ? atoi(s) : 512;
+  }
+  if (R * a.H < many)
+    return launch_check(launch_k(attn_simt_kernel<SIMT_WARPS>, dim3(R, a.H), dim3(SIMT_WARPS * 32), smem, st, a),
+                        "attn_simt");
+  return launch_check(launch_k(attn_simt_kernel<4>, dim3(R, a.H), dim3(4 * 32), smem, st, a), "attn_simt");
 }
 
 // ---------------------------------------------------------------------------

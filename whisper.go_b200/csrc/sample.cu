@@ -9,6 +9,8 @@
 //                      (:1462-1475), beam rebuild (:629-660), all-EOT and
 //                      best-beam repeat stops (:662-691); the KV position
 //                      table of every beam follows its parent (CORRECT mode)
+#include <cooperative_groups.h>
+
 #include "kernels.cuh"
 
 namespace wg {
@@ -21,7 +23,8 @@ namespace {
 // masked when suppress_eot is set. Ends with a CTA barrier, so the row's
 // logits are final for every thread afterwards.
 constexpr int PEN_WIN = 128;
-__device__ void penalty_row(const SampleState& s, int r) {
+// ids outside [c0, c1) are left alone (a CTA that scans only that range of the row)
+__device__ void penalty_range(const SampleState& s, int r, int c0, int c1) {
   __shared__ int hs[PEN_WIN];
   const int n = s.len[r];
   const int start = n > PEN_WIN ? n - PEN_WIN : 0, cnt = n - start;
@@ -31,7 +34,7 @@ __device__ void penalty_row(const SampleState& s, int r) {
   float* lg = s.logits + (int64_t)r * s.V;
   for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
     const int id = hs[i];
-    if (id < 0 || id >= s.V) continue;
+    if (id < 0 || id >= s.V || id < c0 || id >= c1) continue;
     bool first = true;
     for (int j = 0; j < i && first; j++) first = hs[j] != id;
     if (!first) continue;
@@ -40,9 +43,11 @@ __device__ void penalty_row(const SampleState& s, int r) {
     lg[id] = __fsub_rn(lg[id], __fmul_rn(2.0f, (float)c));
   }
   __syncthreads();
-  if (threadIdx.x == 0 && s.suppress_eot && s.eot >= 0 && s.eot < s.V) lg[s.eot] = -INFINITY;
+  if (threadIdx.x == 0 && s.suppress_eot && s.eot >= 0 && s.eot < s.V && s.eot >= c0 && s.eot < c1)
+    lg[s.eot] = -INFINITY;
   __syncthreads();
 }
+__device__ void penalty_row(const SampleState& s, int r) { penalty_range(s, r, 0, s.V); }
 
 struct ArgMax {
   float v;
@@ -65,6 +70,8 @@ __device__ __forceinline__ ArgMax warp_argmax(ArgMax a) {
 // Logit rows are scanned with SCAN_UNROLL independent loads in flight per
 // thread (a row is 51,866 floats; one load at a time made the scan latency-bound).
 constexpr int SCAN_UNROLL = 8;
+
+__device__ void greedy_finish(const SampleState& s, int r, int u, ArgMax all, ArgMax excl, const float* lg);
 
 // ---- greedy ----------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) greedy_kernel(SampleState s) {
@@ -105,6 +112,12 @@ __global__ void __launch_bounds__(1024) greedy_kernel(SampleState s) {
   all = warp_argmax(all);
   excl = warp_argmax(excl);
   if (lane != 0) return;
+  greedy_finish(s, r, u, all, excl, lg);
+}
+
+// The chosen token of row r (all: arg-max of the row, excl: arg-max without
+// EOT) -> SuppressNST re-pick, history append and the stop rules (one thread).
+__device__ void greedy_finish(const SampleState& s, int r, int u, ArgMax all, ArgMax excl, const float* lg) {
   int tok = all.i < 0 ? 0 : all.i;
   if (s.suppress_nst && s.eot >= 0 && s.eot < s.V) {
     if (lg[s.eot] < -s.no_speech_thold && tok == s.eot) tok = excl.i < 0 ? s.eot : excl.i;
@@ -130,6 +143,8 @@ __global__ void __launch_bounds__(1024) greedy_kernel(SampleState s) {
 
 // ---- beam: per-row top-5 of log_softmax(logits / T) ----------------------------
 constexpr int TOPK = 5;
+__device__ void topk_finish(const SampleState& s, int r, const float* lg, float (&fv)[TOPK], int (&fi)[TOPK],
+                            float logZ);
 
 __device__ __forceinline__ void top_insert(float (&v)[TOPK], int (&ix)[TOPK], float nv, int ni) {
   // keep v[0..4] sorted: larger first, lower index first on ties. The new
@@ -256,6 +271,13 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(SampleState s) {
     fi[k] = b.i;
   }
   if (lane != 0) return;
+  topk_finish(s, r, lg, fv, fi, logZ);
+}
+
+// Row r's top-5 (fv, fi: value order, lower index first on ties) and log Z ->
+// topk_tok / topk_lp (one thread), with the exact-tie rerun of the reference scan.
+__device__ void topk_finish(const SampleState& s, int r, const float* lg, float (&fv)[TOPK], int (&fi)[TOPK],
+                            float logZ) {
   bool tie = false;
   for (int k = 0; k + 1 < TOPK; k++) tie |= fi[k + 1] >= 0 && fv[k] == fv[k + 1];
   if (tie) {
@@ -286,6 +308,221 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(SampleState s) {
     s.topk_tok[r * TOPK + k] = fi[k];
     s.topk_lp[r * TOPK + k] = __fsub_rn(fv[k], logZ);
   }
+}
+
+// ---- small batches: each row split over a thread-block cluster --------------------
+// With a few rows per step one CTA per row leaves the GPU idle (a row is
+// V = 51,866 logits); SPLIT CTAs of a cluster each take a contiguous range of
+// the row (penalty, scan), push their partial results into rank 0's shared
+// memory (max also into every rank's), and rank 0 merges them in rank order,
+// which gives the same candidates as one CTA scanning the whole row
+// (first maximum / lower index first on ties). The log-sum-exp is summed per
+// range against the row maximum and then in rank order.
+constexpr int SPLIT = 8;
+constexpr int SPLIT_THREADS = 256;
+
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.aligned;\nbarrier.cluster.wait.aligned;" ::: "memory");
+}
+// generic address of `p` (this CTA's shared memory) in cluster rank `rank`
+template <typename T>
+__device__ __forceinline__ T* cluster_peer(T* p, int rank) {
+  return cooperative_groups::this_cluster().map_shared_rank(p, rank);
+}
+__device__ __forceinline__ int cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return (int)r;
+}
+
+// grid (SPLIT, R), cluster (SPLIT, 1, 1)
+__global__ void __launch_bounds__(SPLIT_THREADS) greedy_split_kernel(SampleState s) {
+  pdl_trigger();
+  cluster_arrive_relaxed();  // peers may be written once every rank runs
+  pdl_wait();
+  const int r = blockIdx.y, u = r;  // B == 1
+  const int rank = cluster_rank();
+  const int chunk = (s.V + SPLIT - 1) / SPLIT, c0 = rank * chunk, c1 = min(s.V, c0 + chunk);
+  __shared__ ArgMax part[2][SPLIT];  // rank 0: every rank's (all, excl)
+  __shared__ ArgMax red[2][SPLIT_THREADS / 32];
+  const bool live = s.utt_done[u] == 0;  // the same for every rank of the cluster
+  ArgMax all{-INFINITY, -1}, excl{-INFINITY, -1};
+  const float* lg = s.logits + (int64_t)r * s.V;
+  if (live) {
+    penalty_range(s, r, c0, c1);
+    for (int i0 = c0 + threadIdx.x; i0 < c1; i0 += SCAN_UNROLL * SPLIT_THREADS) {
+      float x[SCAN_UNROLL];
+#pragma unroll
+      for (int k = 0; k < SCAN_UNROLL; k++) x[k] = i0 + k * SPLIT_THREADS < c1 ? lg[i0 + k * SPLIT_THREADS] : 0.f;
+#pragma unroll
+      for (int k = 0; k < SCAN_UNROLL; k++) {
+        const int i = i0 + k * SPLIT_THREADS;
+        if (i < c1) {
+          const float v = __fmul_rn(x[k], s.inv_temp);
+          all = better(all, ArgMax{v, i});
+          if (i != s.eot) excl = better(excl, ArgMax{v, i});
+        }
+      }
+    }
+    all = warp_argmax(all);
+    excl = warp_argmax(excl);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { red[0][warp] = all; red[1][warp] = excl; }
+    __syncthreads();
+    if (warp == 0) {
+      all = lane < SPLIT_THREADS / 32 ? red[0][lane] : ArgMax{-INFINITY, -1};
+      excl = lane < SPLIT_THREADS / 32 ? red[1][lane] : ArgMax{-INFINITY, -1};
+      all = warp_argmax(all);
+      excl = warp_argmax(excl);
+    }
+  }
+  cluster_wait();
+  if (live && threadIdx.x == 0) {
+    ArgMax* dst = cluster_peer(&part[0][0], 0);
+    dst[rank] = all;
+    dst[SPLIT + rank] = excl;
+  }
+  cluster_sync_all();  // every range's result (and its penalised logits) is in place
+  if (!live || rank != 0 || threadIdx.x != 0) return;
+  ArgMax ga = part[0][0], ge = part[1][0];
+  for (int k = 1; k < SPLIT; k++) {  // rank order = index order: the first maximum wins ties
+    ga = better(ga, part[0][k]);
+    ge = better(ge, part[1][k]);
+  }
+  greedy_finish(s, r, u, ga, ge, lg);
+}
+
+// grid (SPLIT, R), cluster (SPLIT, 1, 1)
+__global__ void __launch_bounds__(SPLIT_THREADS) topk_split_kernel(SampleState s) {
+  pdl_trigger();
+  cluster_arrive_relaxed();
+  pdl_wait();
+  const int r = blockIdx.y, u = r / s.B;
+  const int rank = cluster_rank();
+  const int chunk = (s.V + SPLIT - 1) / SPLIT, c0 = rank * chunk, c1 = min(s.V, c0 + chunk);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = SPLIT_THREADS / 32;
+  __shared__ float cand_v[SPLIT * TOPK];  // rank 0: every rank's top-5
+  __shared__ int cand_i[SPLIT * TOPK];
+  __shared__ float rmax[SPLIT], rsum[SPLIT];  // every rank: all maxima; rank 0: all sums
+  __shared__ float cv[32 * TOPK];
+  __shared__ int ci[32 * TOPK];
+  __shared__ float wred[32];
+  const int n = s.len[r];
+  // the same for every rank of the cluster: finished utterance or hypothesis
+  const bool live = s.utt_done[u] == 0 && !(n > 0 && s.hist[(int64_t)r * s.Tcap + n - 1] == s.eot);
+  const float* lg = s.logits + (int64_t)r * s.V;
+  float tv[TOPK];
+  int ti[TOPK];
+#pragma unroll
+  for (int j = 0; j < TOPK; j++) { tv[j] = -INFINITY; ti[j] = -1; }
+  float mx = -INFINITY;
+  if (live) {
+    penalty_range(s, r, c0, c1);
+    for (int i0 = c0 + threadIdx.x; i0 < c1; i0 += SCAN_UNROLL * SPLIT_THREADS) {
+      float x[SCAN_UNROLL];
+#pragma unroll
+      for (int k = 0; k < SCAN_UNROLL; k++) x[k] = i0 + k * SPLIT_THREADS < c1 ? lg[i0 + k * SPLIT_THREADS] : 0.f;
+#pragma unroll
+      for (int k = 0; k < SCAN_UNROLL; k++) {
+        const int i = i0 + k * SPLIT_THREADS;
+        if (i < c1) {
+          const float v = __fmul_rn(x[k], s.inv_temp);
+          mx = fmaxf(mx, v);
+          top_insert(tv, ti, v, i);
+        }
+      }
+    }
+    // CTA top-5: warps, then warp 0 over the warps' lists
+    for (int k = 0; k < TOPK; k++) {
+      const ArgMax a{tv[0], ti[0]};
+      const ArgMax b = warp_argmax(a);
+      if (a.i == b.i && b.i >= 0) top_pop(tv, ti);
+      if (lane == 0) { cv[warp * TOPK + k] = b.v; ci[warp * TOPK + k] = b.i; }
+    }
+    const float m = warp_max(mx);
+    if (lane == 0) wred[warp] = m;
+    __syncthreads();
+    if (warp == 0) {
+      float mm = lane < nw ? wred[lane] : -INFINITY;
+      mx = warp_max(mm);
+      float lv[TOPK];
+      int li[TOPK];
+#pragma unroll
+      for (int j = 0; j < TOPK; j++) {
+        const bool ok = lane < nw;
+        lv[j] = ok ? cv[lane * TOPK + j] : -INFINITY;
+        li[j] = ok ? ci[lane * TOPK + j] : -1;
+      }
+#pragma unroll
+      for (int k = 0; k < TOPK; k++) {
+        const ArgMax a{lv[0], li[0]};
+        const ArgMax b = warp_argmax(a);
+        if (a.i == b.i && b.i >= 0) top_pop(lv, li);
+        tv[k] = b.v;
+        ti[k] = b.i;
+      }
+    }
+  }
+  cluster_wait();
+  if (live && threadIdx.x == 0) {
+    float* cvd = cluster_peer(cand_v, 0);
+    int* cid = cluster_peer(cand_i, 0);
+    for (int k = 0; k < TOPK; k++) { cvd[rank * TOPK + k] = tv[k]; cid[rank * TOPK + k] = ti[k]; }
+    for (int q = 0; q < SPLIT; q++) cluster_peer(rmax, q)[rank] = mx;
+  }
+  cluster_sync_all();  // every rank's maximum is in its own shared memory
+  float es = 0.f;
+  float gmax = -INFINITY;
+  if (live) {
+    for (int q = 0; q < SPLIT; q++) gmax = fmaxf(gmax, rmax[q]);
+    // terms in float32 (expf, within 2 ulp of the rounded float64 value of
+    // decoder.go:1121-1124); per range, then in rank order
+    for (int i0 = c0 + threadIdx.x; i0 < c1; i0 += SCAN_UNROLL * SPLIT_THREADS) {
+      float x[SCAN_UNROLL];
+#pragma unroll
+      for (int k = 0; k < SCAN_UNROLL; k++) x[k] = i0 + k * SPLIT_THREADS < c1 ? lg[i0 + k * SPLIT_THREADS] : 0.f;
+#pragma unroll
+      for (int k = 0; k < SCAN_UNROLL; k++)
+        if (i0 + k * SPLIT_THREADS < c1) es += expf(__fsub_rn(__fmul_rn(x[k], s.inv_temp), gmax));
+    }
+    es = warp_sum(es);
+    __syncthreads();
+    if (lane == 0) wred[warp] = es;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float tot = 0.f;
+      for (int w = 0; w < nw; w++) tot += wred[w];
+      cluster_peer(rsum, 0)[rank] = tot;
+    }
+  }
+  cluster_sync_all();
+  if (!live || rank != 0 || threadIdx.x != 0) return;
+  float tot = 0.f;
+  for (int q = 0; q < SPLIT; q++) tot += rsum[q];
+  const float logZ = __fadd_rn((float)log((double)tot), gmax);
+  // merge the ranks' lists: repeatedly take the best head (value, then lower index)
+  int head[SPLIT];
+  for (int q = 0; q < SPLIT; q++) head[q] = 0;
+  float fv[TOPK];
+  int fi[TOPK];
+  for (int k = 0; k < TOPK; k++) {
+    int bq = -1;
+    ArgMax b{-INFINITY, -1};
+    for (int q = 0; q < SPLIT; q++) {
+      if (head[q] >= TOPK) continue;
+      const ArgMax c{cand_v[q * TOPK + head[q]], cand_i[q * TOPK + head[q]]};
+      if (c.i < 0) continue;
+      if (bq < 0 || c.v > b.v || (c.v == b.v && c.i < b.i)) { b = c; bq = q; }
+    }
+    if (bq >= 0) head[bq]++;
+    fv[k] = b.v;
+    fi[k] = b.i;
+  }
+  topk_finish(s, r, lg, fv, fi, logZ);
 }
 
 // ---- beam: candidates, prune, rebuild, stops (one CTA per utterance) -------------
@@ -451,11 +688,43 @@ __global__ void reset_kernel(SampleState s, const int* __restrict__ prompt) {
 
 }  // namespace
 
+// A launch of grid (SPLIT, R) in clusters of SPLIT CTAs (programmatic
+// serialisation as launch_k).
+cudaError_t launch_split(void (*kernel)(SampleState), int R, cudaStream_t st, const SampleState& s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(SPLIT, R, 1);
+  cfg.blockDim = dim3(SPLIT_THREADS, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = SPLIT;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kernel, s);
+}
+
+// rows per step up to which a row is split over a cluster (WG_SAMPLE_SPLIT)
+int sample_split_rows() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("WG_SAMPLE_SPLIT");
+    v = (e && *e) ? atoi(e) : 16;
+  }
+  return v;
+}
+
 int launch_sample_step(const SampleState& s, cudaStream_t st) {
+  const bool split = s.R <= sample_split_rows();
   if (s.B <= 1) {
-    WG_CHECK(launch_check(launch_k(greedy_kernel, dim3(s.R), dim3(1024), 0, st, s), "greedy"));
+    if (split) WG_CHECK(launch_check(launch_split(greedy_split_kernel, s.R, st, s), "greedy_split"));
+    else WG_CHECK(launch_check(launch_k(greedy_kernel, dim3(s.R), dim3(1024), 0, st, s), "greedy"));
   } else {
-    WG_CHECK(launch_check(launch_k(topk_kernel, dim3(s.R), dim3(TOPK_THREADS), 0, st, s), "topk"));
+    if (split) WG_CHECK(launch_check(launch_split(topk_split_kernel, s.R, st, s), "topk_split"));
+    else WG_CHECK(launch_check(launch_k(topk_kernel, dim3(s.R), dim3(TOPK_THREADS), 0, st, s), "topk"));
     size_t dyn = (size_t)s.B * (s.Tcap + s.Tmax) * sizeof(int);
     WG_CHECK(launch_check(launch_k(beam_update_kernel, dim3(s.U), dim3(128), dyn, st, s), "beam_update"));
   }
