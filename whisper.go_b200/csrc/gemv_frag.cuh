@@ -111,8 +111,10 @@ __device__ __forceinline__ void epi_store(const Epi& e, int r, int n, float v) {
       e.out[(int64_t)r * e.ldo + n] = v;
       break;
     case EPI_RESID: {
-      float* p = e.out + (int64_t)r * e.ldo + n;
-      *p = __fadd_rn(*p, __fadd_rn(v, e.bias ? e.bias[n] : 0.f));
+      // x += (acc + b): one writer per element, so the fire-and-forget
+      // reduction rounds exactly like load-add-store without waiting on x
+      const float add = __fadd_rn(v, e.bias ? e.bias[n] : 0.f);
+      asm volatile("red.global.add.f32 [%0], %1;" ::"l"(e.out + (int64_t)r * e.ldo + n), "f"(add) : "memory");
       break;
     }
     case EPI_GELU_F16:
