@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-steps", type=int, default=2)
+    ap.add_argument("--jobs", type=int, default=1,
+                    help="concurrent decode jobs per GPU, each with its own stream and host thread, "
+                         "splitting the GPU's utterances")
     ap.add_argument("--layers", type=int, default=0,
                     help="decoder layers (default: the config's); fewer only for small profiler captures")
     return ap.parse_args()
@@ -249,12 +252,41 @@ def main():
     encs = [hnp[u] for u in range(U)]
     params = wgdec.DecoderParams(prompt=PROMPT, beam_size=cfg["beam"], max_tokens=args.tokens, mode=mode,
                                  suppress_eot=True)
-    job = wgdec.Job(dec, U, T_ENC, params)
-    job.upload(encs)  # resident in HBM before the timed region
+    # J concurrent jobs split the utterances; each has its own stream, CUDA
+    # graph and workspace, and a host thread drives it, so the kernels of one
+    # fill the GPU while the other's kernels drain
+    J = max(1, min(args.jobs, U))
+    shares = [U // J + (1 if j < U % J else 0) for j in range(J)]
+    offs = [sum(shares[:j]) for j in range(J)]
+    jobs = [wgdec.Job(dec, shares[j], T_ENC, params) for j in range(J)]
+    for j in range(J):
+        jobs[j].upload(encs[offs[j]:offs[j] + shares[j]])  # resident in HBM before the timed region
+    job = jobs[0]
+
+    def run_all(fn):
+        if J == 1:
+            fn(jobs[0])
+            return
+        import threading
+        errs = []
+
+        def body(jb):
+            try:
+                fn(jb)
+            except Exception as ex:  # re-raised on the main thread
+                errs.append(ex)
+        ts = [threading.Thread(target=body, args=(jb,)) for jb in jobs]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+        if errs:
+            raise errs[0]
 
     def decode_once():
-        job.start()
-        job.run()
+        for jb in jobs:
+            jb.start()
+        run_all(lambda jb: jb.run())
 
     for _ in range(args.warmup):
         decode_once()
@@ -262,14 +294,24 @@ def main():
     clocks = Clocks(local)
     clocks.start()
     launches0 = wgdec.kernel_launch_count()
-    job.timer_start()
+    t_wall = time.perf_counter()
+    for jb in jobs:
+        jb.timer_start()
     for _ in range(args.steps):
         decode_once()
-    ms = job.timer_stop()
+    # device time of each job's stream; with several jobs the region spans
+    # from the first start to the last stop, so also take the host wall clock
+    ms = max(jb.timer_stop() for jb in jobs)
+    if J > 1:
+        ms = max(ms, (time.perf_counter() - t_wall) * 1e3)
     launches = wgdec.kernel_launch_count() - launches0
     clk = clocks.stop()
-    toks, lens, _ = job.result()
-    tokens_per_decode = float(np.sum(lens - len(PROMPT)))
+    tokens_per_decode = 0.0
+    rows = 0
+    for jb in jobs:
+        toks, lens, _ = jb.result()
+        tokens_per_decode += float(np.sum(lens - len(PROMPT)))
+        rows += jb.stats()[1]
     dist.barrier()
     ms_max = dist.max(ms)
     total_tokens = dist.sum(tokens_per_decode * args.steps)
@@ -278,7 +320,7 @@ def main():
     # roofline: per-class device time of one step's launches (CUDA events on the job stream)
     peak, peak_kind = peaks()
     classes = {}
-    steps_done, rows, _ = job.stats()
+    steps_done, _, _ = job.stats()
     per_step_launches = {"gemv": 6 * cfg["L"], "self_attn": cfg["L"], "cross_attn": cfg["L"], "logits": 1}
     for k in ("gemv", "self_attn", "cross_attn", "logits"):
         t, b = job.time_kernel(k, iters=3)
@@ -305,30 +347,38 @@ def main():
                      "measured_ms": step_ms, "frac": (step_bytes / 8e12 * 1e3) / step_ms,
                      "frac_of_measured_peak": (step_bytes / (peak * 1e6)) / step_ms}
 
-    job.close()  # free its KV caches before the end-to-end job allocates its own
+    for jb in jobs:
+        jb.close()  # free their KV caches before the end-to-end jobs allocate their own
     # end to end through the public API: pinned host -> device, decode, tokens back
     e2e = None
     if not args.no_e2e:
-        e2e_job = wgdec.Job(dec, U, T_ENC, params)
-        e2e_job.upload(encs)
-        e2e_job.start()
-        e2e_job.run()
-        e2e_job.result()
+        e2e_jobs = [wgdec.Job(dec, shares[j], T_ENC, params) for j in range(J)]
+        out = [None] * J
+
+        def e2e_one(j):
+            jb = e2e_jobs[j]
+            jb.upload(encs[offs[j]:offs[j] + shares[j]])
+            jb.start()
+            jb.run()
+            out[j] = jb.result()
+
+        jobs = e2e_jobs
+        run_all(lambda jb: e2e_one(e2e_jobs.index(jb)))
         dist.barrier()
-        e2e_job.timer_start()
+        for jb in e2e_jobs:
+            jb.timer_start()
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            e2e_job.upload(encs)
-            e2e_job.start()
-            e2e_job.run()
-            t2, l2, _ = e2e_job.result()
-        e_ms = e2e_job.timer_stop()
+            run_all(lambda jb: e2e_one(e2e_jobs.index(jb)))
+        e_ms = max(jb.timer_stop() for jb in e2e_jobs)
         wall = (time.perf_counter() - t0) * 1e3
         e_ms = dist.max(max(e_ms, wall))
+        d2h = sum(int(o[0].nbytes + o[1].nbytes) for o in out) + 4 * U
         e2e = {"value": total_tokens / (e_ms / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": int(U * T_ENC * cfg["d"] * 4),
-               "d2h_bytes_per_step": int(t2.nbytes + l2.nbytes + 4 * U)}
-        e2e_job.close()
+               "d2h_bytes_per_step": d2h}
+        for jb in e2e_jobs:
+            jb.close()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -343,7 +393,8 @@ def main():
                            "beam": cfg["beam"], "rows_per_step": rows, "tokens_per_decode": args.tokens,
                            "mode": args.mode, "kv_dtype": "f16", "t_enc": T_ENC,
                            "l2": "inputs larger than L2 (per-step KV + weights >> 126 MB)",
-                           "parallelism": "dp%d (utterances, no collective)" % world},
+                           "parallelism": "dp%d (utterances, no collective)" % world,
+                           "jobs_per_gpu": J},
                 "roofline": roofline, "step_roofline": step_roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "clocks": clk,
                 "gpu_launches": int(launches)}
