@@ -4,10 +4,11 @@ file:line citations (paths inside the wxcdart/whisper.go module).
 
 The reference is Go and cannot run here, so its test vectors are restated:
 each entry rebuilds the test's input bytes exactly as the Go test does and
-records the values the Go test asserts. When the reference tree is present
-(REF env var, default /root/reference) every citation is checked: the quoted
+records the values the Go test asserts. When the REF environment variable
+names a checkout of the reference, every citation is checked: the quoted
 source fragment must appear on the cited line, so a transcription that drifts
-from the reference fails loudly. Run: python tests/golden/make_golden.py
+from the reference fails loudly.
+Run: REF=<whisper.go checkout> python tests/golden/make_golden.py
 """
 import json
 import os
@@ -15,13 +16,13 @@ import pathlib
 import struct
 
 HERE = pathlib.Path(__file__).resolve().parent
-REF = pathlib.Path(os.environ.get("REF", "/root/reference"))
+REF = pathlib.Path(os.environ["REF"]) if os.environ.get("REF") else None
 
 
 def cite(path, line, fragment):
     """Checks that `fragment` occurs on line `line` of the reference file."""
-    f = REF / path
-    if f.exists():
+    f = REF / path if REF else None
+    if f is not None and f.exists():
         lines = f.read_text().splitlines()
         if fragment not in lines[line - 1]:
             raise SystemExit("citation mismatch: %s:%d does not contain %r" % (path, line, fragment))
