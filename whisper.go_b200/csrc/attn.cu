@@ -79,11 +79,16 @@ __global__ void __launch_bounds__(NW * 32) attn_simt_kernel(SimtArgs a) {
   __shared__ float qs[64];
   const float* qr = a.q + (int64_t)r * a.ldq + h * hd;
   for (int c = threadIdx.x; c < 64; c += blockDim.x) qs[c] = c < hd ? qr[c] : 0.f;
+  // the row's position table staged once, so a K or V load never waits on a
+  // table load from global memory
+  int* tsm = reinterpret_cast<int*>(red + SIMT_WARPS + SIMT_WARPS * 64);  // [n] (tbl only)
+  if (a.tbl)
+    for (int t = threadIdx.x; t < n; t += blockDim.x) tsm[t] = a.tbl[(int64_t)r * a.tbl_ld + t];
   __syncthreads();
   const float scale = (float)(1.0 / sqrt((double)hd));
   const int sub = lane >> 3, dl = (lane & 7) * 8;  // 4 positions per warp step, 8 dims per lane
   auto slab_of = [&](int t) -> int64_t {
-    return a.tbl ? (int64_t)a.tbl[(int64_t)r * a.tbl_ld + t] : (int64_t)(r / a.rows_per_slab);
+    return a.tbl ? (int64_t)tsm[t] : (int64_t)(r / a.rows_per_slab);
   };
   // scores: each warp step covers 4 positions (8 lanes x 8 dims each); the
   // table lookups and K rows of SIMT_UNROLL steps are loaded before use
@@ -233,7 +238,8 @@ __global__ void __launch_bounds__(NW * 32) attn_simt_kernel(SimtArgs a) {
 }
 
 int launch_simt(const SimtArgs& a, int R, int n_max, cudaStream_t st) {
-  size_t smem = (size_t)(((n_max + 3) & ~3) + SIMT_WARPS + SIMT_WARPS * 64) * 4;
+  // scores [n] | warp reduction [SIMT_WARPS] | warp outputs [SIMT_WARPS][64] | position table [n]
+  size_t smem = (size_t)(((n_max + 3) & ~3) + SIMT_WARPS + SIMT_WARPS * 64 + (a.tbl ? n_max : 0)) * 4;
   if (smem > 48 * 1024) {
     set_error("attention: %d positions exceed the SIMT kernel's shared memory", n_max);
     return WG_ERR_UNSUPPORTED;
