@@ -108,3 +108,13 @@ def test_decoder_params_mapping():
                              suppress_eot=True)
     c2 = p2.to_c()
     assert (c2.beam_size, c2.max_tokens, c2.mode, c2.suppress_eot) == (5, 17, wgdec.MODE_REF_COMPAT, 1)
+
+
+def test_noalloc_matmul_rejects_bad_arguments_before_any_device_work():
+    """wg_model_matmul_noalloc checks its arguments first: a null model (or a
+    bad layer / matrix index) is rejected with WG_ERR_INVALID and a message,
+    without touching a device."""
+    L = wgdec.lib()
+    rc = L.wg_model_matmul_noalloc(None, 0, 0, 0, None, 0, 0, None, 0, None, 1)
+    assert rc == ERR_INVALID
+    assert last_error() == "wg_model_matmul_noalloc: bad argument"
