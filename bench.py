@@ -4,16 +4,18 @@ One "step" is one whole Decode of the batch: cross K/V precompute for every
 utterance, then the token loop (224 steps, beam 5 by default) on the GPU.
 Workload (default): BASELINE.json configs[4], large-v3-shaped decoder
 (d=1280, 32 layers, 20 heads, vocab 51866), Q8_0 weights from seeded
-N(0, 0.02), 64 utterances per GPU with synthetic N(0,1) encoder outputs
+N(0, 0.02), a batch of 64 utterances with synthetic N(0,1) encoder outputs
 [1500, 1280], beam 5, 224 steps (EOT suppressed so every utterance runs the
-full length), CORRECT-mode decoding. N GPUs (torchrun) each decode their own
-64 utterances: weak scaling, no collective on the token loop.
+full length), CORRECT-mode decoding. With N GPUs (torchrun) the 64
+utterances are sharded over the ranks (64/N each, rank r takes utterances
+r, r+N, ...): strong scaling of the one batch, no collective on the token
+loop. `--weak` instead gives every rank its own full batch.
 
-  value : decoder tokens/s (utterance-steps/s, beams not counted), inputs
-          resident in HBM, device time from CUDA events on the job's stream,
-          max over ranks
+  value : decoder tokens/s of the whole job (utterance-steps/s summed over
+          all GPUs, beams not counted), inputs resident in HBM, device time
+          from CUDA events on each job's stream, max over ranks
   e2e   : same metric through the public C-ABI job API with pinned host
-          encoder outputs uploaded and tokens read back every step
+          encoder outputs uploaded and tokens read back every decode
   --impl reference : the CPU restatement of whisper.go's decoder (oracle),
           timed on the host cores, on a bounded sample of the same workload
 """
@@ -49,7 +51,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=5)
-    ap.add_argument("--utterances", type=int, default=0, help="per GPU (default: the config's)")
+    ap.add_argument("--utterances", type=int, default=0,
+                    help="utterances of the batch (default: the config's); sharded over the GPUs unless --weak")
+    ap.add_argument("--weak", action="store_true",
+                    help="weak scaling: every GPU decodes its own --utterances (default: one batch sharded)")
     ap.add_argument("--tokens", type=int, default=STEPS_PER_DECODE)
     ap.add_argument("--mode", default="correct", choices=["correct", "ref_compat"])
     ap.add_argument("--no-e2e", action="store_true")
@@ -70,9 +75,15 @@ def dist_env():
     return rank, world, local
 
 
-def utterance_ids(rank, U):
-    """Utterances of one rank: each GPU decodes its own U (weak scaling, no data-path collective)."""
-    return [rank * U + u for u in range(U)]
+def utterance_ids(rank, world, U, weak=False):
+    """Global ids of the utterances one rank decodes (no data-path collective).
+
+    Strong scaling (default): the batch of U utterances is sharded round-robin,
+    rank r taking r, r + world, ... Weak scaling: every rank decodes its own U.
+    """
+    if weak:
+        return [rank * U + u for u in range(U)]
+    return list(range(rank, U, world))
 
 
 class Dist:
@@ -218,10 +229,14 @@ def run_reference(args, cfg, rank, world):
             vals.append(cb)
     v = statistics.median([c["value"] for c in vals])
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak" if args.weak else "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init weights, N(0,1) encoder)",
-            "config": {"workload": "config %d: %s" % (args.config, cfg["name"]), "utterances_per_gpu": U,
-                       "beam": cfg["beam"], "tokens": args.tokens},
+            "config": {"workload": "config %d: %s, tokens/s extrapolated from %d token steps of %d utterances "
+                                   "on the host cores" % (args.config, cfg["name"], args.cpu_sample_steps,
+                                                          min(U, threads)),
+                       "utterances": U, "beam": cfg["beam"], "tokens": args.tokens,
+                       "sample_token_steps": args.cpu_sample_steps},
             "cpu_baseline": {"kind": "port", "cores": threads, "sample": vals[-1]["sample"], "value": v},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -237,7 +252,11 @@ def main():
     import numpy as np
     import wgdec
     dist = Dist(world, local)
-    U = args.utterances or cfg["U"]
+    U_batch = args.utterances or cfg["U"]
+    ids = utterance_ids(rank, world, U_batch, args.weak)
+    if not ids:
+        raise SystemExit("bench: %d utterances cannot be sharded over %d GPUs (use --weak)" % (U_batch, world))
+    U = len(ids)  # this rank's utterances
     if args.layers:
         cfg = dict(cfg, L=args.layers)
     mode = wgdec.MODE_CORRECT if args.mode == "correct" else wgdec.MODE_REF_COMPAT
@@ -247,7 +266,7 @@ def main():
     import torch
     host = torch.empty((U, T_ENC, cfg["d"]), dtype=torch.float32, pin_memory=True)
     hnp = host.numpy()
-    for u, uid in enumerate(utterance_ids(rank, U)):
+    for u, uid in enumerate(ids):
         hnp[u] = model.encoder_output(uid, T_ENC)
     encs = [hnp[u] for u in range(U)]
     params = wgdec.DecoderParams(prompt=PROMPT, beam_size=cfg["beam"], max_tokens=args.tokens, mode=mode,
@@ -373,10 +392,10 @@ def main():
         e_ms = max(jb.timer_stop() for jb in e2e_jobs)
         wall = (time.perf_counter() - t0) * 1e3
         e_ms = dist.max(max(e_ms, wall))
-        d2h = sum(int(o[0].nbytes + o[1].nbytes) for o in out) + 4 * U
+        d2h = dist.sum(sum(int(o[0].nbytes + o[1].nbytes + o[2].nbytes) for o in out))
+        h2d = dist.sum(U * T_ENC * cfg["d"] * 4)  # encoder outputs of all ranks
         e2e = {"value": total_tokens / (e_ms / 1e3), "unit": "tokens/s",
-               "h2d_bytes_per_step": int(U * T_ENC * cfg["d"] * 4),
-               "d2h_bytes_per_step": d2h}
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
         for jb in e2e_jobs:
             jb.close()
 
@@ -387,9 +406,13 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16xf16->f32",
+                "higher_is_better": True, "scaling": "weak" if args.weak else "strong", "vs_baseline": None,
+                "dtype": "f16xf16->f32",
+                "value_is": "whole-job decoder tokens/s summed over all %d GPU(s)" % world,
+                "value_per_gpu": value / world,
                 "data": "synthetic (seeded random-init weights, N(0,1) encoder outputs)",
-                "config": {"workload": "config %d: %s" % (args.config, cfg["name"]), "utterances_per_gpu": U,
+                "config": {"workload": "config %d: %s" % (args.config, cfg["name"]), "utterances": U_batch,
+                           "utterances_per_gpu": U_batch if args.weak else -(-U_batch // world),
                            "beam": cfg["beam"], "rows_per_step": rows, "tokens_per_decode": args.tokens,
                            "mode": args.mode, "kv_dtype": "f16", "t_enc": T_ENC,
                            "l2": "inputs larger than L2 (per-step KV + weights >> 126 MB)",

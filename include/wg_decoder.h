@@ -6,8 +6,8 @@
  *         (internal/model/interfaces.go:22-25)
  * the CPU implementation in internal/model/decoder.go (WhisperDecoder,
  * decoder.go:61-82) and the tensor ops it calls (internal/ml/matmul_q8.go,
- * attention.go, ops.go). A cgo package binds these symbols; see
- * INTEGRATION.md for the binding.
+ * attention.go, ops.go). A cgo package (go/internal/cuda in this
+ * repository) binds these symbols behind model.Decoder.
  *
  * Conventions
  *  - Every function returns an int status (WG_OK == 0). No C++ exception
@@ -213,10 +213,14 @@ int wg_matmul_test(uint32_t qtype, const void* raw, int rows, int cols,
  *   out   : device fp32 [rows][ldo], ldo >= N
  *   wait  : nonzero: wait for the stream and report a CUDA error or an
  *           expired device-side wait (WG_ERR_DEVICE_FLAG) before returning;
- *           zero: return once the kernel is enqueued.
+ *           zero: return once the kernel is enqueued (an expired wait is
+ *           then reported by the next call on the device with wait != 0:
+ *           these calls keep their own error word, apart from decode jobs).
  * The first call on a device also does set-up (it looks up the scratch
  * array's device address with that device current), so make it before any
- * stream capture begins. All calls on one device share the scratch: calls
+ * stream capture begins; the set-up is repeated only if the device's CUDA
+ * context was destroyed and created again. All calls on one device share
+ * the scratch: calls
  * whose kernels can overlap in time (different streams or host threads)
  * race and give wrong results; issue them in one stream or one at a time.
  * The caller's current device is restored before returning. */

@@ -358,7 +358,7 @@ OR_API int or_matmul(uint32_t qtype, const void* raw, int rows, int cols,
   if (rb < 0) return WG_ERR_UNSUPPORTED;
   const uint8_t* w = (const uint8_t*)raw;
   int64_t total = (int64_t)m * rows;
-#pragma omp parallel for schedule(static) num_threads(g_inner_threads) if (g_inner_threads > 1 && total >= 4096)
+#pragma omp parallel for schedule(static) num_threads(g_inner_threads) if (g_inner_threads > 1 && total >= 512)
   for (int64_t t = 0; t < total; t++) {
     int i = (int)(t / rows), j = (int)(t % rows);
     out[t] = or_dot_row(qtype, w + (int64_t)j * rb, a + (int64_t)i * cols, cols);
@@ -583,6 +583,7 @@ typedef struct {
 typedef struct {
   float* kv;       /* [L][2][H][ctx][hd] (decoder.go:346) */
   float *x, *xln, *q, *k, *v, *attn, *out, *mlph, *logits, *scores;
+  float* xscores; /* [H][T_enc] cross-attention scores, one row per head (inner threads) */
   int scores_cap;
 } ostate;
 
@@ -596,10 +597,11 @@ static void st_init(ostate* s, const om* M, int T_enc) {
   s->logits = (float*)calloc(M->V, 4);
   s->scores_cap = (T_enc > M->ctx ? T_enc : M->ctx);
   s->scores = (float*)calloc(s->scores_cap, 4);
+  s->xscores = g_inner_threads > 1 ? (float*)calloc((size_t)M->H * T_enc, 4) : NULL;
 }
 static void st_free(ostate* s) {
   free(s->kv); free(s->x); free(s->xln); free(s->q); free(s->k); free(s->v);
-  free(s->attn); free(s->out); free(s->mlph); free(s->logits); free(s->scores);
+  free(s->attn); free(s->out); free(s->mlph); free(s->logits); free(s->scores); free(s->xscores);
 }
 
 static void matvec(const wg_matrix* w, const float* x, float* y) {
@@ -674,20 +676,24 @@ static int forward(const om* M, ostate* s, const ocross* cr, int T_enc, int toke
     /* K_c/V_c [T,d] viewed as [H,T,hd] by reshape (:950-951): head h is the
      * column block h*hd..h*hd+hd-1 of every row, i.e. stride d between rows.
      * or_attention wants [T,hd] per head, so gather per head. */
+    /* heads are independent: with inner threads each head has its own
+     * scores row (same arithmetic as one thread doing them in turn) */
+#pragma omp parallel for schedule(static) num_threads(g_inner_threads) if (s->xscores && H > 1)
     for (int h = 0; h < H; h++) {
+      float* sc = s->xscores ? s->xscores + (int64_t)h * T_enc : s->scores;
       /* scores */
       float scale = (float)(1.0 / sqrt((double)hd));
       for (int t = 0; t < T_enc; t++) {
         float acc = 0;
         const float* kr = cr[l].k + (int64_t)t * d + h * hd;
         for (int c = 0; c < hd; c++) acc += s->q[h * hd + c] * kr[c];
-        s->scores[t] = acc;
+        sc[t] = acc;
       }
-      for (int t = 0; t < T_enc; t++) s->scores[t] *= scale;
-      or_softmax_fast(s->scores, T_enc);
+      for (int t = 0; t < T_enc; t++) sc[t] *= scale;
+      or_softmax_fast(sc, T_enc);
       for (int c = 0; c < hd; c++) {
         float acc = 0;
-        for (int t = 0; t < T_enc; t++) acc += s->scores[t] * cr[l].v[(int64_t)t * d + h * hd + c];
+        for (int t = 0; t < T_enc; t++) acc += sc[t] * cr[l].v[(int64_t)t * d + h * hd + c];
         s->attn[h * hd + c] = acc;
       }
     }

@@ -31,10 +31,11 @@ def _rank(rank, world, port, q):
     d.barrier()
     mx = d.max(10.0 + rank)      # per-rank "ms": the job time is the slowest rank's
     tot = d.sum(100.0 * (rank + 1))  # per-rank tokens: the job's tokens are the sum
-    ids = bench.utterance_ids(rank, 4)
+    ids = bench.utterance_ids(rank, world, 64)             # one batch sharded (strong scaling)
+    weak = bench.utterance_ids(rank, world, 4, weak=True)  # every rank its own batch
     d.barrier()
     d.close()
-    q.put((rank, mx, tot, ids))
+    q.put((rank, mx, tot, ids, weak))
 
 
 def test_two_gloo_ranks_time_and_shard():
@@ -52,4 +53,6 @@ def test_two_gloo_ranks_time_and_shard():
     assert [r[1] for r in res] == [11.0, 11.0]
     assert [r[2] for r in res] == [300.0, 300.0]
     ids = res[0][3] + res[1][3]
-    assert sorted(ids) == list(range(8)) and len(set(res[0][3]) & set(res[1][3])) == 0
+    assert sorted(ids) == list(range(64)) and len(res[0][3]) == len(res[1][3]) == 32
+    weak = res[0][4] + res[1][4]
+    assert sorted(weak) == list(range(8)) and len(set(res[0][4]) & set(res[1][4])) == 0

@@ -76,13 +76,22 @@ def test_matches_the_allocating_entry_point_twice(setup, which):
 
 
 def test_rejects_shapes_beyond_the_scratch(setup):
+    """mlp.0 (1024 x 256) at 2048 rows: 64 output tiles, so a K split of 2 or
+    more would need 64 x ks x 256 x 128 floats, beyond the 2 Mi of the
+    scratch; the call must refuse it, or (where occupancy leaves the K
+    unsplit and no scratch is needed) give the allocating entry point's result."""
     torch, model, dec = setup
-    # q|k|v (768 x 256) at 1024 rows: 24 output tiles x 4 K splits x 256 x 128 floats > 2 Mi
-    x16 = torch.zeros((1024, 256), dtype=torch.float16, device="cuda:0")
-    rc, _ = _noalloc(torch, dec, 0, 0, x16, 768)
-    assert rc == ERR_INVALID
-    msg = _last_error()
-    assert "wg_model_matmul_noalloc" in msg and "scratch" in msg
+    raw, n, k = _weights(model, 0, 4)
+    x = np.random.default_rng(7).standard_normal((2048, k)).astype(np.float16)
+    x16 = torch.from_numpy(x).to("cuda:0")
+    rc, out = _noalloc(torch, dec, 0, 4, x16, n)
+    if rc == ERR_INVALID:
+        msg = _last_error()
+        assert "wg_model_matmul_noalloc" in msg and "scratch" in msg
+    else:
+        assert rc == 0, _last_error()
+        ref = wgdec.matmul("Q8_0", raw, n, k, x.astype(np.float32), path=3)
+        np.testing.assert_allclose(out.cpu().numpy(), ref, atol=ATOL, rtol=RTOL)
 
 
 def test_rejects_bad_layouts(setup):

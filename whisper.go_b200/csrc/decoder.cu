@@ -1127,33 +1127,67 @@ int wg_job_time_kernel(wg_job* J, int kclass, int iters, double* ms, double* byt
 // from this fixed array instead of allocating a workspace: it exists for
 // callers that may not allocate device memory while they run. The array is
 // part of the module's device image (one copy per device); its address is
-// looked up once per device with that device current. Every call on a device
-// shares it, so calls whose kernels overlap in time race.
+// looked up with the device current on the first call in each CUDA context
+// of a device (again only if that context was destroyed and recreated).
+// Every call on a device shares it, so calls whose kernels overlap in time
+// race. Expired waits of these calls are recorded in their own error word,
+// not in the one the decode jobs share.
 namespace wg {
 static __device__ __align__(256) float g_noalloc_scratch[WG_NOALLOC_SCRATCH_FLOATS];
+static __device__ int g_noalloc_error;
 namespace {
 constexpr int NOALLOC_MAX_DEV = 64;
 std::mutex g_noalloc_mu;
-float* g_noalloc_ptr[NOALLOC_MAX_DEV] = {};
+struct NoallocDev {
+  void* ctx = nullptr;  // CUDA context the addresses belong to
+  float* scratch = nullptr;
+  int* err = nullptr;
+};
+NoallocDev g_noalloc[NOALLOC_MAX_DEV];
 
-// Device address of the scratch array on device dev (which must be current).
-int noalloc_scratch(int dev, float** out) {
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<CtxGetCurrentFn>(p);
+    return (CtxGetCurrentFn) nullptr;
+  }();
+  return fn;
+}
+
+// Device addresses of the scratch array and the error word on device dev
+// (which must be current).
+int noalloc_symbols(int dev, NoallocDev* out) {
   if (dev < 0 || dev >= NOALLOC_MAX_DEV) {
     set_error("wg_model_matmul_noalloc: device %d out of range", dev);
     return WG_ERR_INVALID;
   }
+  CUcontext ctx = nullptr;
+  CtxGetCurrentFn get = ctx_get_current_fn();
+  if (!get || get(&ctx) != CUDA_SUCCESS || !ctx) {
+    set_error("wg_model_matmul_noalloc: no current CUDA context on device %d", dev);
+    return WG_ERR_CUDA;
+  }
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  NoallocDev& nd = g_noalloc[dev];
+  if (nd.ctx != (void*)ctx || !nd.scratch || !nd.err) {
     float* p = nullptr;
+    int* w = nullptr;
     cudaError_t e = cudaGetSymbolAddress((void**)&p, g_noalloc_scratch);
-    if (e != cudaSuccess || !p) {
+    if (e == cudaSuccess) e = cudaGetSymbolAddress((void**)&w, g_noalloc_error);
+    if (e != cudaSuccess || !p || !w) {
       set_error("wg_model_matmul_noalloc: cudaGetSymbolAddress of the scratch array failed: %s",
                 cudaGetErrorString(e));
       return WG_ERR_CUDA;
     }
-    g_noalloc_ptr[dev] = p;
+    nd.ctx = (void*)ctx;
+    nd.scratch = p;
+    nd.err = w;
   }
-  *out = g_noalloc_ptr[dev];
+  *out = nd;
   return WG_OK;
 }
 }  // namespace
@@ -1183,16 +1217,17 @@ extern "C" int wg_model_matmul_noalloc(wg_model* m, int replica, int layer, int 
   int prev = -1;
   WG_CHECK_CUDA(cudaGetDevice(&prev));
   WG_CHECK_CUDA(cudaSetDevice(dm.dev));
-  float* ws = nullptr;
-  int rc = noalloc_scratch(dm.dev, &ws);
+  NoallocDev sym;
+  int rc = noalloc_symbols(dm.dev, &sym);
   if (rc == WG_OK) {
     Epi e;
     e.mode = EPI_F32;
     e.out = out;
     e.ldo = ldo;
     e.N = W.rows;
-    e.split_ws = ws;
+    e.split_ws = sym.scratch;
     e.split_ws_floats = WG_NOALLOC_SCRATCH_FLOATS;
+    e.err_word = sym.err;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     rc = launch_matmul(W, reinterpret_cast<const __half*>(x16), ldx, rows, e, st, 3);
     if (rc == WG_ERR_INVALID) {
@@ -1202,7 +1237,17 @@ extern "C" int wg_model_matmul_noalloc(wg_model* m, int replica, int layer, int 
     }
     if (rc == WG_OK && wait) {
       rc = wait_stream(st);
-      if (rc == WG_OK) rc = check_wait_flags();
+      int w = 0;
+      if (rc == WG_OK && cudaMemcpyFromSymbol(&w, g_noalloc_error, sizeof(int)) != cudaSuccess) {
+        set_error("wg_model_matmul_noalloc: reading the error word failed");
+        rc = WG_ERR_CUDA;
+      }
+      if (rc == WG_OK && w) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g_noalloc_error, &z, sizeof(int));
+        set_error("wg_model_matmul_noalloc: a bounded wait of the tcgen05 kernel expired (code 0x%x)", w);
+        rc = WG_ERR_DEVICE_FLAG;
+      }
     }
   }
   cudaSetDevice(prev);

@@ -243,6 +243,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const TcLayout L = tc_layout(QT, NR);
   const int S = L.stages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* const errw = e.err_word ? e.err_word : &g_tc_error;
   const int tile0 = blockIdx.x * 8;
   const int r0 = blockIdx.y * NR;
   const int nk_all = W.cols / TC_BK;
@@ -340,7 +341,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (lane < TC_LOAD_LANES && kl < nk) {
         const int s = kl % TC_DQ_NS;
         const uint32_t ph = (uint32_t)(kl / TC_DQ_NS) & 1u;
-        ok = mbar_wait(RAW_EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 1, &g_tc_error);
+        ok = mbar_wait(RAW_EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 1, errw);
         if (ok) issue_weights(kl);
       }
       if (!__all_sync(0xffffffffu, ok)) break;
@@ -355,7 +356,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (lane < lanes && kl < nk) {
         const int s = kl % S;
         const uint32_t ph = (uint32_t)(kl / S) & 1u;
-        ok = mbar_wait(EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 2, &g_tc_error);
+        ok = mbar_wait(EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 2, errw);
         if (ok) {
           mbar_arrive_tx(FULL(s), L.b_bytes);
           tma_2d(base + L.b0 + s * L.b_bytes, &xmap, kstage(kl) * TC_BK, r0, FULL(s));
@@ -373,7 +374,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                              | ((uint32_t)(TC_BM >> 4) << 24);  // M
       for (int kl = 0; kl < nk; kl++) {
         const int s = kl % S;
-        if (!mbar_wait(FULL(s), (uint32_t)(kl / S) & 1u, abort_flag, (kl << 8) | 3, &g_tc_error)) break;
+        if (!mbar_wait(FULL(s), (uint32_t)(kl / S) & 1u, abort_flag, (kl << 8) | 3, errw)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t at = tmem + TC_A_COL + 32u * (uint32_t)s;  // A in tensor memory
         const uint64_t bd = sw128_desc(base + L.b0 + s * L.b_bytes);
@@ -411,7 +412,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t ph = (uint32_t)(kl / S) & 1u;
       const int rs = kl % TC_DQ_NS;
       bool ok = mbar_wait2(RAW_FULL(rs), (uint32_t)(kl / TC_DQ_NS) & 1u, EMPTY(s), ph ^ 1u, abort_flag,
-                           (kl << 8) | 4, &g_tc_error);
+                           (kl << 8) | 4, errw);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       const uint32_t ro = rs * L.raw_bytes;
@@ -517,7 +518,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                        : reinterpret_cast<float*>(sm);
   bool done_ok = true;
   if (warp < TC_DQ_WARPS) {
-    done_ok = mbar_wait(DONE, 0, abort_flag, 6, &g_tc_error);
+    done_ok = mbar_wait(DONE, 0, abort_flag, 6, errw);
     done_ok = __all_sync(0xffffffffu, done_ok);
   }
   if (warp < TC_DQ_WARPS && done_ok) {
@@ -601,6 +602,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_drain(RAW_FULL(lane), (uint32_t)(issued_w[lane] / TC_DQ_NS) & 1u);
   }
   if (warp == TC_MMA_WARP) {
+    // after an abort nobody may have waited for DONE: the MMAs issued before
+    // it (DONE tracks them all) must finish writing tensor memory before it
+    // is released
+    if (*abort_flag && lane == 0) mbar_drain(DONE, 0);
     __syncwarp();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");

@@ -40,6 +40,9 @@ struct Epi {
   // (no other launch may use it concurrently); contents need no initialisation
   float* split_ws = nullptr;
   int64_t split_ws_floats = 0;
+  // tcgen05 path: the word an expired bounded wait records its code in
+  // (device memory; nullptr: the tcgen05 kernels' shared word, tc_error_word)
+  int* err_word = nullptr;
   // Small-batch path only (matmul_fuses_input_ln): the activations are
   // LayerNorm(ln_x) of ln_d-wide fp32 rows, normalised inside the GEMV with
   // the LayerNorm kernel's arithmetic (X is not read).

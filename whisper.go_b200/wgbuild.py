@@ -36,15 +36,25 @@ def _run(cmd, cwd=None):
 
 
 def build_lib(force=False, verbose_ptxas=False):
+    """Compiles every csrc/*.cu for sm_100a (one nvcc process per file, in
+    parallel; objects under _build/) and links libwgdec.so."""
     srcs = sorted((PKG / "csrc").glob("*.cu"))
     deps = srcs + sorted((PKG / "csrc").glob("*.cuh")) + [ROOT / "include" / "wg_decoder.h"]
     if not force and not _stale(LIB, deps):
         return ""
-    cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
-           "-Xcompiler", "-fPIC", "-shared", "-o", str(LIB), *map(str, srcs)]
+    from concurrent.futures import ThreadPoolExecutor
+    obj_dir = ROOT / "_build"
+    obj_dir.mkdir(exist_ok=True)
+    flags = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC"]
     if verbose_ptxas:
-        cmd[1:1] = ["-Xptxas", "-v"]
-    return _run(cmd)
+        flags = ["-Xptxas", "-v", *flags]
+    objs = [obj_dir / (s.stem + ".o") for s in srcs]
+    with ThreadPoolExecutor(max_workers=max(1, min(len(srcs), os.cpu_count() or 1))) as ex:
+        logs = list(ex.map(lambda so: _run([NVCC, *flags, "-c", "-o", str(so[1]), str(so[0])]), zip(srcs, objs)))
+    tmp = LIB.with_suffix(".so.tmp")
+    logs.append(_run([NVCC, *ARCH, "-shared", "-o", str(tmp), *map(str, objs)]))
+    os.replace(tmp, LIB)  # the library is never seen half-written
+    return "".join(logs)
 
 
 def build_gen(force=False):
