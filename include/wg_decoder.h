@@ -109,19 +109,37 @@ typedef struct wg_model_desc {
 } wg_model_desc;
 
 /* The DecoderParams fields the reference decoder reads
- * (internal/model/interfaces.go:75-90), plus two switches of this build. */
+ * (internal/model/interfaces.go:75-90), plus switches of this build. */
 typedef struct wg_decode_params {
   int32_t beam_size;        /* <= 1: greedy (decoder.go:406) */
   float temperature;        /* 0 means 1.0 (decoder.go:416-419, :530-533) */
   int32_t attempt;          /* temperature-schedule attempt: T += 0.2*attempt (decoder.go:435,:537) */
-  float logprob_thold;      /* > 0 with !no_fallback enables top-p fallback: WG_ERR_UNSUPPORTED */
+  float logprob_thold;      /* > 0 with !no_fallback: greedy steps whose best log-prob is below
+                               -logprob_thold draw from the top-p (0.9) nucleus instead
+                               (decoder.go:1036-1056, sampler :1251-1378) */
   float no_speech_thold;    /* used by suppress_nst (decoder.go:1016-1034) */
   int32_t no_fallback;
   int32_t max_tokens;       /* <= 0: n_text_ctx; capped at n_text_ctx - P (decoder.go:421-430) */
   int32_t suppress_nst;
   int32_t mode;             /* WG_MODE_REF_COMPAT or WG_MODE_CORRECT */
   int32_t suppress_eot;     /* 1: EOT never selected (fixed-length benchmark runs); 0: reference */
+  /* Seed of the top-p draws. The reference draws rand.Float32() from Go's
+   * unseeded global source; here the draw of utterance u (its index in the
+   * job) at its generated-token step t is wg_uniform(seed, u, t), so a
+   * decode is reproducible and the CPU oracle makes the same draws. */
+  uint64_t seed;
 } wg_decode_params;
+
+/* The top-p draw: SplitMix64's output function (Steele, Lea & Flood 2014) of
+ * seed ^ (u + 1) * 0x9E3779B97F4A7C15 ^ (t + 1) * 0xD1B54A32D192ED03, its top
+ * 24 bits scaled to [0, 1) (the 24-bit resolution of Go's Float32). */
+static inline float wg_uniform(uint64_t seed, uint32_t u, uint32_t t) {
+  uint64_t z = seed ^ ((uint64_t)u + 1) * 0x9E3779B97F4A7C15ull ^ ((uint64_t)t + 1) * 0xD1B54A32D192ED03ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (float)(z >> 40) * (1.0f / 16777216.0f);
+}
 
 typedef struct wg_model wg_model;
 typedef struct wg_job wg_job;
@@ -137,6 +155,9 @@ int wg_kernel_launch_count(int64_t* n);
  * replica of the weights to each listed device (n_dev >= 1). */
 int wg_model_create(const wg_model_desc* desc, const int* devices, int n_dev, wg_model** out);
 int wg_model_destroy(wg_model* m);
+/* The vocabulary's end-of-text id (SetVocabulary, decoder.go:85-95); jobs
+ * created afterwards stop on it. */
+int wg_model_set_eot(wg_model* m, int eot);
 /* Device bytes of one replica's weights (quant blocks as uploaded). */
 int wg_model_weight_bytes(const wg_model* m, int64_t* bytes);
 
@@ -149,6 +170,18 @@ int wg_job_create(wg_model* m, int U, int T_enc, const int32_t* prompt, int P,
 /* Host -> device copy of U encoder outputs, each [T_enc, d] fp32 row-major
  * (enc[u] points at utterance u). */
 int wg_job_upload_encoder(wg_job* j, const float* const* enc);
+/* Device of utterance u (the device whose memory wg_job_upload_encoder_device
+ * expects its encoder output in). */
+int wg_job_utterance_device(const wg_job* j, int u, int* device);
+/* Encoder -> decoder hand-off on the device (the encoder output that
+ * internal/model/encoder.go:265-332 returns, left on the GPU by a GPU
+ * encoder): enc[u] is DEVICE memory [T_enc, d] fp32 on utterance u's device.
+ * The job's stream first waits for everything enqueued so far on `stream`
+ * (a cudaStream_t of the encoder; NULL: the legacy default stream is
+ * synchronised), then copies device to device; the call returns without
+ * waiting for the copies, and the encoder buffers must stay valid until
+ * wg_job_start returns. Replaces wg_job_upload_encoder for that case. */
+int wg_job_upload_encoder_device(wg_job* j, const float* const* enc, void* stream);
 /* Cross K/V precompute for every layer, prompt prefill (CORRECT mode) and
  * reset of the beam / token state. Must follow an upload. */
 int wg_job_start(wg_job* j);
@@ -159,6 +192,11 @@ int wg_job_step(wg_job* j, int max_steps, int* done);
 /* tokens: U x (P + max_tokens) int32 (prompt included, like the reference's
  * final token slice), lens: U, scores: U (beam log-prob sum; 0 for greedy). */
 int wg_job_result(wg_job* j, int32_t* tokens, int32_t* lens, float* scores);
+/* Every hypothesis of every utterance as it stands after the steps run so
+ * far (the beams slice of decodeBeamSearch, decoder.go:545-552 and :629-660,
+ * in its order: beams[0] is the best). tokens: U x B x (P + max_tokens),
+ * lens and scores: U x B (B = 1 for greedy). */
+int wg_job_beams(wg_job* j, int32_t* tokens, int32_t* lens, float* scores);
 int wg_job_cancel(wg_job* j);
 /* Device timer on the job's own stream(s): which = 0 records the start
  * event, which = 1 records the stop event, waits, and returns in *ms the
@@ -193,6 +231,17 @@ int wg_dequant_test(uint32_t qtype, const void* raw, int64_t n, float* out);
  * Replaces ml.MatMulQuantTransBInto (ml/matmul_q8.go:93-119). */
 int wg_matmul_test(uint32_t qtype, const void* raw, int rows, int cols,
                    const float* x, int m, float* out, int path);
+
+/* The token-selection kernels of one step on given logits (kernel-level
+ * parity): R rows of V fp32 logits, each row an utterance whose history is
+ * hist[r][0..n_hist) (prompt included; the repetition penalty reads it,
+ * decoder.go:1140-1167). Greedy (params->beam_size <= 1): out_tok[r] =
+ * sampleGreedyWithScratch's token (decoder.go:996-1059) with the top-p
+ * fallback when params enable it, drawing wg_uniform(seed, r, step).
+ * Beam: out_tok[r*5 + k], out_lp[r*5 + k] = topKTokensWithScratch's five
+ * (decoder.go:1068-1136). */
+int wg_sample_test(const float* logits, int R, int V, const int32_t* hist, int n_hist, int eot,
+                   const wg_decode_params* params, int step, int32_t* out_tok, float* out_lp);
 
 /* ---- allocation-free matmul (no reference counterpart) --------------------
  * For callers that may not allocate device memory once they are running

@@ -534,6 +534,113 @@ OR_API int or_sample_greedy(const float* logits, int V, int eot, float temperatu
   return maxIdx;
 }
 
+/* scaled values desc, lower index first on equal values (the reference's
+ * sort.Slice is unstable; exactly equal values are measure-zero) */
+static const float* g_sort_key;
+static int cmp_desc(const void* a, const void* b) {
+  int i = *(const int*)a, j = *(const int*)b;
+  float x = g_sort_key[i], y = g_sort_key[j];
+  if (x > y) return -1;
+  if (x < y) return 1;
+  return i < j ? -1 : (i > j);
+}
+static void sort_desc(int* idx, int n, const float* key) {
+  /* qsort with a file-scope key: the oracle's decodes are parallel over
+   * utterances, so serialise the (rare) fallback sorts */
+#pragma omp critical(or_sort)
+  {
+    g_sort_key = key;
+    qsort(idx, (size_t)n, sizeof(int), cmp_desc);
+  }
+}
+
+/* model/decoder.go:1251-1378 (sampleTopPFromLogitsWithScratch): scaled
+ * logits, logZ (float32 sum of float64 exps), the best min(512, V) by a
+ * replace-min scan, sorted descending; cumulative float32 probabilities up to
+ * topP (a full sort of the row when those 512 do not reach it); then the draw
+ * r = u01 * cumSum walks the same cumulative sum. u01 replaces the
+ * reference's rand.Float32() (unseeded math/rand): wg_uniform(seed, u, t). */
+OR_API int or_sample_topp(const float* logits, int V, float temperature, float topP, float u01) {
+  if (V <= 0) return 0;
+  float it = inv_temp(temperature);
+  float* sc = (float*)malloc((size_t)V * 4);
+  int* idx = (int*)malloc((size_t)V * 4);
+  float scaledMax = logits[0] * it;
+  for (int i = 0; i < V; i++) {
+    sc[i] = logits[i] * it;
+    idx[i] = i;
+    if (sc[i] > scaledMax) scaledMax = sc[i];
+  }
+  float expSum = 0;
+  for (int i = 0; i < V; i++) expSum += (float)exp((double)(sc[i] - scaledMax));
+  float logZ = (float)log((double)expSum) + scaledMax;
+  int limit = V < 512 ? V : 512;
+  int n = 0, minPos = -1;
+  float minScore = 0;
+  for (int i = 0; i < V; i++) {
+    if (n < limit) {
+      idx[n++] = i;
+      if (minPos < 0 || sc[i] < minScore) { minPos = n - 1; minScore = sc[i]; }
+      continue;
+    }
+    if (sc[i] > minScore) {
+      idx[minPos] = i;
+      minPos = 0;
+      minScore = sc[idx[0]];
+      for (int j = 1; j < n; j++)
+        if (sc[idx[j]] < minScore) { minScore = sc[idx[j]]; minPos = j; }
+    }
+  }
+  sort_desc(idx, n, sc);
+  int topCount = 0;
+  float cumSum = 0;
+  for (int i = 0; i < n; i++) {
+    cumSum += (float)exp((double)(sc[idx[i]] - logZ));
+    topCount = i + 1;
+    if (cumSum >= topP) break;
+  }
+  if (cumSum < topP && n < V) { /* full sort */
+    for (int i = 0; i < V; i++) idx[i] = i;
+    sort_desc(idx, V, sc);
+    n = V;
+    topCount = 0;
+    cumSum = 0;
+    for (int i = 0; i < n; i++) {
+      cumSum += (float)exp((double)(sc[idx[i]] - logZ));
+      topCount = i + 1;
+      if (cumSum >= topP) break;
+    }
+  }
+  int tok = idx[topCount > 0 ? topCount - 1 : 0];
+  if (topCount > 0) {
+    float r = u01 * cumSum, run = 0;
+    for (int i = 0; i < topCount; i++) {
+      run += (float)exp((double)(sc[idx[i]] - logZ));
+      if (run >= r) { tok = idx[i]; break; }
+    }
+  }
+  free(sc);
+  free(idx);
+  return tok;
+}
+
+/* wg_uniform of the ABI header (the seeded top-p draw), for the tests. */
+OR_API float or_uniform(uint64_t seed, uint32_t u, uint32_t t) { return wg_uniform(seed, u, t); }
+
+/* The top-p fallback test of sampleGreedyWithScratch (decoder.go:1036-1056):
+ * returns 1 when the chosen token's log-prob (at temperature T) is below
+ * -logprob_thold, so the step draws from the nucleus instead. */
+OR_API int or_topp_fallback(const float* logits, int V, int chosen, float temperature, float logprob_thold) {
+  float it = inv_temp(temperature);
+  float scaledMax = -INFINITY;
+  for (int i = 0; i < V; i++)
+    if (logits[i] * it > scaledMax) scaledMax = logits[i] * it;
+  float expSum = 0;
+  for (int i = 0; i < V; i++) expSum += (float)exp((double)(logits[i] * it - scaledMax));
+  float logZ = (float)log((double)expSum) + scaledMax;
+  return logits[chosen] * it - logZ < -logprob_thold;
+}
+
 /* model/decoder.go:1068-1136 (topKTokensWithScratch): replace-min scan, then
  * logZ = log(sum float32(exp(float64(s - max)))) + max, lp = s - logZ,
  * sorted by lp descending (stable here; Go's sort.Slice is unstable, which
@@ -744,10 +851,51 @@ static int prefill(const om* M, ostate* s, const ocross* cr, int T_enc, const in
   return 0;
 }
 
+/* Optional record of a decode for the parity tests: the margin of every
+ * step's decision (how far the logits could move before another token or
+ * beam order would be chosen) and, for beam search, the beams after every
+ * step. Not part of the reference; it only observes the loops below. */
+typedef struct {
+  float* margin;        /* [max_tokens] */
+  int32_t* topp;        /* [max_tokens] 1 where the step drew from the top-p nucleus */
+  int32_t* beam_toks;   /* [max_tokens][B][stride] */
+  int32_t* beam_lens;   /* [max_tokens][B] */
+  float* beam_scores;   /* [max_tokens][B] */
+  int stride;           /* P + max_tokens */
+  int steps;            /* out: steps executed */
+} otrace;
+
+/* Top-2 gap of scaled logits (optionally without one id). */
+static float top2_gap(const float* lg, int V, float it, int skip) {
+  float a = -INFINITY, b = -INFINITY;
+  for (int i = 0; i < V; i++) {
+    if (i == skip) continue;
+    float s = lg[i] * it;
+    if (s > a) { b = a; a = s; }
+    else if (s > b) b = s;
+  }
+  return b == -INFINITY ? FLT_MAX : a - b;
+}
+
+/* Decision margin of sampleGreedyWithScratch on one row (decoder.go:1006-1034). */
+static float greedy_margin(const float* lg, int V, int eot, float temperature, int suppress_nst, float thold) {
+  float it = inv_temp(temperature);
+  int arg = or_sample_greedy(lg, V, eot, temperature, 0, 0.f);
+  float m;
+  if (suppress_nst && eot >= 0 && eot < V && arg == eot) {
+    float d = fabsf(lg[eot] + thold); /* the threshold test itself */
+    m = lg[eot] < -thold ? top2_gap(lg, V, it, eot) : top2_gap(lg, V, it, -1);
+    if (d < m) m = d;
+  } else {
+    m = top2_gap(lg, V, it, -1);
+  }
+  return m;
+}
+
 /* model/decoder.go:413-525 (decodeGreedy) without a vocabulary (no
  * compression-ratio retry, :490). */
 static int decode_greedy(const om* M, const ocross* cr, int T_enc, const int32_t* prompt, int P,
-                         const wg_decode_params* p, int32_t* toks, int* len, int max_steps) {
+                         const wg_decode_params* p, int32_t* toks, int* len, int max_steps, otrace* tr, int utt) {
   ostate s;
   st_init(&s, M, T_enc);
   int mt = max_tokens_for(M, p, P);
@@ -764,6 +912,12 @@ static int decode_greedy(const om* M, const ocross* cr, int T_enc, const int32_t
     or_apply_penalty(cur, M->V, toks, n, 2.0f, 128); /* :454-457 */
     if (p->suppress_eot && M->m->eot >= 0 && M->m->eot < M->V) cur[M->m->eot] = -INFINITY;
     int next = or_sample_greedy(cur, M->V, M->m->eot, temp, p->suppress_nst, p->no_speech_thold);
+    if (tr) tr->margin[steps] = greedy_margin(cur, M->V, M->m->eot, temp, p->suppress_nst, p->no_speech_thold);
+    if (p->logprob_thold > 0 && !p->no_fallback && temp > 0 &&      /* :1036-1056 */
+        or_topp_fallback(cur, M->V, next, temp, p->logprob_thold)) {
+      next = or_sample_topp(cur, M->V, temp, 0.9f, wg_uniform(p->seed, (uint32_t)utt, (uint32_t)steps));
+      if (tr) tr->topp[steps] = 1;
+    }
     toks[n++] = next;
     steps++;
     if (next == M->m->eot) break;     /* :470 */
@@ -774,6 +928,7 @@ static int decode_greedy(const om* M, const ocross* cr, int T_enc, const int32_t
   free(cur);
   st_free(&s);
   *len = n;
+  if (tr) tr->steps = steps;
   return rc;
 }
 
@@ -782,7 +937,7 @@ typedef struct { int parent; float score; int32_t token; float logprob, norm; in
 /* model/decoder.go:528-726 (decodeBeamSearch) without a vocabulary. */
 static int decode_beam(const om* M, const ocross* cr, int T_enc, const int32_t* prompt, int P,
                        const wg_decode_params* p, int32_t* out_toks, int* out_len, float* out_score,
-                       int max_steps) {
+                       int max_steps, otrace* tr) {
   int B = p->beam_size, ctxw = P + max_tokens_for(M, p, P) + 1;
   int mt = max_tokens_for(M, p, P);
   float temp = temperature_for(p);
@@ -790,9 +945,9 @@ static int decode_beam(const om* M, const ocross* cr, int T_enc, const int32_t* 
   ostate* st = (ostate*)calloc(B, sizeof(ostate));
   ostate* tmpst = (ostate*)calloc(B, sizeof(ostate));
   int32_t* toks = (int32_t*)malloc((size_t)B * ctxw * 4);
-  int32_t* ntoks = (int32_t*)malloc((size_t)B * ctxw * 4);
+  int32_t* ntoks = (int32_t*)calloc((size_t)B * ctxw, 4);
   int* len = (int*)malloc(B * 4);
-  int* nlen = (int*)malloc(B * 4);
+  int* nlen = (int*)calloc(B, 4);
   float* score = (float*)calloc(B, 4);
   float* nscore = (float*)calloc(B, 4);
   ocand* cands = (ocand*)malloc((size_t)B * 6 * sizeof(ocand));
@@ -810,8 +965,10 @@ static int decode_beam(const om* M, const ocross* cr, int T_enc, const int32_t* 
   }
   if (p->mode == WG_MODE_CORRECT)
     for (int b = 0; b < B; b++) tmpst[b].kv = (float*)malloc(kv_elems * 4);
-  for (int step = 0; !rc && step < mt && step < max_steps; step++) {
+  int step = 0;
+  for (step = 0; !rc && step < mt && step < max_steps; step++) {
     int nc = 0;
+    float margin = FLT_MAX;
     for (int b = 0; b < B; b++) {
       int32_t* tb = toks + b * ctxw;
       if (len[b] > 0 && tb[len[b] - 1] == eot) { /* :580-591 */
@@ -835,6 +992,10 @@ static int decode_beam(const om* M, const ocross* cr, int T_enc, const int32_t* 
       if (p->suppress_eot && eot >= 0 && eot < M->V) cur[eot] = -INFINITY;
       int32_t tk[5]; float lp[5];
       int k = or_topk(cur, M->V, 5, temp, tk, lp); /* :606-608 */
+      if (tr) { /* the 5th / 6th boundary of this row's candidates */
+        int32_t tk6[6]; float lp6[6];
+        if (or_topk(cur, M->V, 6, temp, tk6, lp6) == 6 && lp6[4] - lp6[5] < margin) margin = lp6[4] - lp6[5];
+      }
       for (int j = 0; j < k; j++) {                /* :610-622 */
         int newLen = len[b] + 1;
         float ns = score[b] + lp[j];
@@ -850,6 +1011,12 @@ static int decode_beam(const om* M, const ocross* cr, int T_enc, const int32_t* 
       cands[j + 1] = c;
     }
     int nb = nc < B ? nc : B;
+    if (tr) { /* order of the kept candidates and the kept / dropped boundary */
+      int lim = nc < B + 1 ? nc : B + 1;
+      for (int i = 0; i + 1 < lim; i++)
+        if (cands[i].norm - cands[i + 1].norm < margin) margin = cands[i].norm - cands[i + 1].norm;
+      tr->margin[step] = margin;
+    }
     /* rebuild beams (:629-660) */
     for (int i = 0; i < nb; i++) {
       const ocand* c = &cands[i];
@@ -865,9 +1032,20 @@ static int decode_beam(const om* M, const ocross* cr, int T_enc, const int32_t* 
     if (p->mode == WG_MODE_CORRECT)
       for (int i = 0; i < nb; i++) { float* t = st[i].kv; st[i].kv = tmpst[i].kv; tmpst[i].kv = t; }
     memcpy(toks, ntoks, (size_t)B * ctxw * 4);
-    memcpy(len, nlen, B * 4);
-    memcpy(score, nscore, B * 4);
+    memcpy(len, nlen, (size_t)B * 4);
+    memcpy(score, nscore, (size_t)B * 4);
     B = nb; /* beams = nextBeams (len(bestCandidates)) */
+    if (tr) {
+      const int B0 = p->beam_size;
+      for (int b = 0; b < B0; b++) {
+        int32_t* dst = tr->beam_toks + ((int64_t)step * B0 + b) * tr->stride;
+        memset(dst, 0, (size_t)tr->stride * 4);
+        if (b < B) memcpy(dst, toks + b * ctxw, (size_t)(len[b] < tr->stride ? len[b] : tr->stride) * 4);
+        tr->beam_lens[step * B0 + b] = b < B ? len[b] : 0;
+        tr->beam_scores[step * B0 + b] = b < B ? score[b] : 0.f;
+      }
+      tr->steps = step + 1;
+    }
     int allEOT = 1; /* :662-672 */
     for (int b = 0; b < B; b++) if (len[b] == 0 || toks[b * ctxw + len[b] - 1] != eot) { allEOT = 0; break; }
     if (allEOT) break;
@@ -896,16 +1074,55 @@ static int decode_beam(const om* M, const ocross* cr, int T_enc, const int32_t* 
 static int check_params(const om* M, const wg_decode_params* p, int P) {
   if (P <= 0) return WG_ERR_INVALID;
   if (p->mode != WG_MODE_REF_COMPAT && p->mode != WG_MODE_CORRECT) return WG_ERR_INVALID;
-  if (p->logprob_thold > 0 && !p->no_fallback) return WG_ERR_UNSUPPORTED;
   if (P > M->ctx) return WG_ERR_INVALID;
   return 0;
 }
 
 /* Decode U utterances (each like one Decode call), utterances in parallel
  * over nthreads host threads. tokens: U x (P + max_tokens). */
+static int decode_all(const wg_model_desc* m, const float* const* enc, int U, int T_enc,
+                      const int32_t* prompt, int P, const wg_decode_params* p, int32_t* tokens,
+                      int32_t* lens, float* scores, int nthreads, otrace* trs);
+
 OR_API int or_decode(const wg_model_desc* m, const float* const* enc, int U, int T_enc,
                      const int32_t* prompt, int P, const wg_decode_params* p, int32_t* tokens,
                      int32_t* lens, float* scores, int nthreads) {
+  return decode_all(m, enc, U, T_enc, prompt, P, p, tokens, lens, scores, nthreads, NULL);
+}
+
+/* or_decode plus the per-step record of every utterance (otrace): margins
+ * [U][max_tokens]; for beam search the beams after each step, tokens
+ * [U][max_tokens][B][P + max_tokens], lens and scores [U][max_tokens][B];
+ * steps [U] = steps executed. */
+OR_API int or_decode_trace(const wg_model_desc* m, const float* const* enc, int U, int T_enc,
+                           const int32_t* prompt, int P, const wg_decode_params* p, int32_t* tokens,
+                           int32_t* lens, float* scores, int nthreads, float* margins, int32_t* beam_toks,
+                           int32_t* beam_lens, float* beam_scores, int32_t* steps, int32_t* topp) {
+  om M;
+  int rc = om_init(&M, m);
+  if (rc) return rc;
+  int mt = max_tokens_for(&M, p, P), B = p->beam_size > 1 ? p->beam_size : 1, stride = P + mt;
+  otrace* trs = (otrace*)calloc(U, sizeof(otrace));
+  for (int u = 0; u < U; u++) {
+    trs[u].margin = margins + (int64_t)u * mt;
+    trs[u].topp = topp + (int64_t)u * mt;
+    for (int i = 0; i < mt; i++) { trs[u].margin[i] = FLT_MAX; trs[u].topp[i] = 0; }
+    if (B > 1) {
+      trs[u].beam_toks = beam_toks + (int64_t)u * mt * B * stride;
+      trs[u].beam_lens = beam_lens + (int64_t)u * mt * B;
+      trs[u].beam_scores = beam_scores + (int64_t)u * mt * B;
+    }
+    trs[u].stride = stride;
+  }
+  rc = decode_all(m, enc, U, T_enc, prompt, P, p, tokens, lens, scores, nthreads, trs);
+  for (int u = 0; u < U; u++) steps[u] = trs[u].steps;
+  free(trs);
+  return rc;
+}
+
+static int decode_all(const wg_model_desc* m, const float* const* enc, int U, int T_enc,
+                      const int32_t* prompt, int P, const wg_decode_params* p, int32_t* tokens,
+                      int32_t* lens, float* scores, int nthreads, otrace* trs) {
   om M;
   int rc = om_init(&M, m);
   if (rc) return rc;
@@ -921,9 +1138,9 @@ OR_API int or_decode(const wg_model_desc* m, const float* const* enc, int U, int
     float sc = 0;
     int32_t* buf = (int32_t*)calloc((size_t)stride + 1, 4);
     if (p->beam_size > 1)
-      r = decode_beam(&M, cr, T_enc, prompt, P, p, buf, &len, &sc, 1 << 30);
+      r = decode_beam(&M, cr, T_enc, prompt, P, p, buf, &len, &sc, 1 << 30, trs ? &trs[u] : NULL);
     else
-      r = decode_greedy(&M, cr, T_enc, prompt, P, p, buf, &len, 1 << 30);
+      r = decode_greedy(&M, cr, T_enc, prompt, P, p, buf, &len, 1 << 30, trs ? &trs[u] : NULL, u);
     if (r) {
 #pragma omp atomic write
       err = r;
@@ -996,8 +1213,8 @@ OR_API int or_bench_steps(const wg_model_desc* m, int U, int T_enc, const int32_
     int32_t* buf = (int32_t*)calloc((size_t)P + mt + 1, 4);
     int len = 0;
     float sc = 0;
-    if (p->beam_size > 1) decode_beam(&M, crs[u], T_enc, prompt, P, p, buf, &len, &sc, n_steps);
-    else decode_greedy(&M, crs[u], T_enc, prompt, P, p, buf, &len, n_steps);
+    if (p->beam_size > 1) decode_beam(&M, crs[u], T_enc, prompt, P, p, buf, &len, &sc, n_steps, NULL);
+    else decode_greedy(&M, crs[u], T_enc, prompt, P, p, buf, &len, n_steps, NULL, u);
     done += len - P;
     free(buf);
   }

@@ -56,6 +56,15 @@ def lib():
         P = ctypes.POINTER(wgdec.WgModelDesc)
         L.or_decode.argtypes = [P, ctypes.POINTER(fp), ctypes.c_int, ctypes.c_int, ip, ctypes.c_int,
                                 ctypes.POINTER(wgdec.WgDecodeParams), ip, ip, fp, ctypes.c_int]
+        L.or_decode_trace.argtypes = [P, ctypes.POINTER(fp), ctypes.c_int, ctypes.c_int, ip, ctypes.c_int,
+                                      ctypes.POINTER(wgdec.WgDecodeParams), ip, ip, fp, ctypes.c_int, fp, ip, ip,
+                                      fp, ip, ip]
+        L.or_sample_topp.restype = ctypes.c_int
+        L.or_sample_topp.argtypes = [fp, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_float]
+        L.or_uniform.restype = ctypes.c_float
+        L.or_uniform.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32]
+        L.or_topp_fallback.restype = ctypes.c_int
+        L.or_topp_fallback.argtypes = [fp, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float]
         L.or_teacher_forced.argtypes = [P, fp, ctypes.c_int, ip, ctypes.c_int, ip, ctypes.c_int, ctypes.c_int, fp]
         L.or_bench_steps.argtypes = [P, ctypes.c_int, ctypes.c_int, ip, ctypes.c_int,
                                      ctypes.POINTER(wgdec.WgDecodeParams), ctypes.c_int, ctypes.c_int,
@@ -160,6 +169,21 @@ def sample_greedy(logits, eot, temperature, suppress_nst=False, no_speech_thold=
     return int(lib().or_sample_greedy(_f(lg), lg.size, eot, temperature, int(suppress_nst), no_speech_thold))
 
 
+def sample_topp(logits, temperature, u01, top_p=0.9) -> int:
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    return int(lib().or_sample_topp(_f(lg), lg.size, temperature, top_p, u01))
+
+
+def uniform(seed: int, u: int, t: int) -> float:
+    """wg_uniform (include/wg_decoder.h): the seeded draw of the top-p sampler."""
+    return float(lib().or_uniform(seed & 0xFFFFFFFFFFFFFFFF, u, t))
+
+
+def topp_fallback(logits, chosen, temperature, logprob_thold) -> bool:
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    return bool(lib().or_topp_fallback(_f(lg), lg.size, int(chosen), temperature, logprob_thold))
+
+
 def topk(logits, k, temperature):
     lg = np.ascontiguousarray(logits, dtype=np.float32)
     tok = np.zeros(k, dtype=np.int32)
@@ -190,6 +214,36 @@ def decode(model, encs, params: "wgdec.DecoderParams", n_ctx: int, threads: int 
                            ctypes.byref(cp), toks.ctypes.data_as(ip), lens.ctypes.data_as(ip), _f(scores),
                            threads), "decode")
     return toks, lens, scores
+
+
+def decode_trace(model, encs, params: "wgdec.DecoderParams", n_ctx: int, threads: int = 1):
+    """decode() plus the per-step record: dict with tokens, lens, scores,
+    margins [U, max_tokens] (the decision margin of each step: top-2 logit gap
+    for greedy; for beams the smallest of every live row's 5th/6th logit gap
+    and the gaps among the best B+1 candidates' normalised scores), steps [U],
+    and for beam search beams_tokens [U, max_tokens, B, stride], beams_lens
+    and beams_scores [U, max_tokens, B] (the beams after each step)."""
+    arrs = [np.ascontiguousarray(e, dtype=np.float32) for e in encs]
+    ptrs = (fp * len(arrs))(*[_f(a) for a in arrs])
+    pr = np.asarray(params.prompt, dtype=np.int32)
+    mt = wgdec.max_tokens_for(params, n_ctx)
+    U, B, stride = len(arrs), max(1, int(params.beam_size)), len(pr) + mt
+    toks = np.zeros((U, stride), dtype=np.int32)
+    lens = np.zeros(U, dtype=np.int32)
+    scores = np.zeros(U, dtype=np.float32)
+    margins = np.zeros((U, max(mt, 1)), dtype=np.float32)
+    btoks = np.zeros((U, max(mt, 1), B, stride), dtype=np.int32)
+    blens = np.zeros((U, max(mt, 1), B), dtype=np.int32)
+    bscores = np.zeros((U, max(mt, 1), B), dtype=np.float32)
+    steps = np.zeros(U, dtype=np.int32)
+    topp = np.zeros((U, max(mt, 1)), dtype=np.int32)
+    cp = params.to_c()
+    _check(lib().or_decode_trace(_desc(model), ptrs, U, arrs[0].shape[0], pr.ctypes.data_as(ip), len(pr),
+                                 ctypes.byref(cp), toks.ctypes.data_as(ip), lens.ctypes.data_as(ip), _f(scores),
+                                 threads, _f(margins), btoks.ctypes.data_as(ip), blens.ctypes.data_as(ip),
+                                 _f(bscores), steps.ctypes.data_as(ip), topp.ctypes.data_as(ip)), "decode_trace")
+    return dict(tokens=toks, lens=lens, scores=scores, margins=margins[:, :mt], steps=steps, topp=topp[:, :mt],
+                beams_tokens=btoks[:, :mt], beams_lens=blens[:, :mt], beams_scores=bscores[:, :mt])
 
 
 def teacher_forced(model, enc, prompt, forced, mode, n_vocab) -> np.ndarray:

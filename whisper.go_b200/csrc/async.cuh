@@ -48,13 +48,14 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 // Bounded wait: false (abort flag raised, code recorded in *err) once the
 // limits pass, or when another warp of the CTA has aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int code, int* err) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int code, int* err,
+                                          uint64_t limit_ns = WAIT_NS) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 0; i < WAIT_LIMIT; i++) {
     if (mbar_try(bar, parity)) return true;
     if (*abort) return false;
-    if (global_ns() - t0 > WAIT_NS) break;
+    if (global_ns() - t0 > limit_ns) break;
   }
   *abort = 1;
   atomicCAS(err, 0, code);
@@ -73,7 +74,7 @@ __device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity) {
 // Waits for two barriers; both try_waits are issued before either result is
 // used, so their latencies overlap.
 __device__ __forceinline__ bool mbar_wait2(uint32_t bar_a, uint32_t par_a, uint32_t bar_b, uint32_t par_b,
-                                           volatile int* abort, int code, int* err) {
+                                           volatile int* abort, int code, int* err, uint64_t limit_ns = WAIT_NS) {
   bool da = false, db = false;
   uint64_t t0 = 0;
   for (uint32_t i = 0; i < WAIT_LIMIT; i++) {
@@ -91,7 +92,7 @@ __device__ __forceinline__ bool mbar_wait2(uint32_t bar_a, uint32_t par_a, uint3
     if (da && db) return true;
     if (*abort) return false;
     if (i == 0) t0 = global_ns();
-    else if (global_ns() - t0 > WAIT_NS) break;
+    else if (global_ns() - t0 > limit_ns) break;
   }
   *abort = 1;
   atomicCAS(err, 0, code | (da ? 0 : 0x10) | (db ? 0 : 0x20));

@@ -404,7 +404,7 @@ int build_devjob(wg_job* J, DevModel* dm, const std::vector<int>& utt, DevJob** 
   cudaMemsetAsync(j->h16, 0, (size_t)R * j->ld4 * 2, j->st);
   if (j->ldd != d) cudaMemsetAsync(j->enc16, 0, (size_t)U * T * j->ldd * 2, j->st);
   // integer / float state
-  const size_t n_ints = (size_t)R * j->Tcap * 2 + (size_t)R * j->Tmax * 2 + (size_t)R * 16 + (size_t)U * 2 + 8;
+  const size_t n_ints = (size_t)R * j->Tcap * 2 + (size_t)R * j->Tmax * 2 + (size_t)R * 16 + (size_t)U * 3 + 8;
   const size_t n_floats = (size_t)R * 8;
   if ((rc = dalloc(&j->ints, n_ints)) || (rc = dalloc(&j->floats, n_floats)) ||
       (rc = dalloc(&j->split_ws, (size_t)TC_SPLIT_WS_FLOATS)))
@@ -426,6 +426,11 @@ int build_devjob(wg_job* J, DevModel* dm, const std::vector<int>& utt, DevJob** 
     s.suppress_nst = p.suppress_nst;
     s.no_speech_thold = p.no_speech_thold;
     s.suppress_eot = p.suppress_eot;
+    // top-p fallback of greedy steps (decoder.go:1036-1037): LogprobThold > 0,
+    // !NoFallback, temperature > 0; beam search never falls back
+    s.topp = j->B <= 1 && p.logprob_thold > 0.f && !p.no_fallback && temp > 0.f;
+    s.logprob_thold = p.logprob_thold;
+    s.seed = p.seed;
   }
   s.correct_mode = J->mode == WG_MODE_CORRECT;
   s.hist = take((size_t)R * j->Tcap);
@@ -441,6 +446,8 @@ int build_devjob(wg_job* J, DevModel* dm, const std::vector<int>& utt, DevJob** 
   s.topk_tok = take((size_t)R * 5);
   s.utt_done = take(U);
   s.utt_steps = take(U);
+  int* utt_id = take(U);
+  s.utt_id = utt_id;
   s.n_done = take(1);
   s.pos = take(1);
   s.step = take(1);
@@ -452,7 +459,8 @@ int build_devjob(wg_job* J, DevModel* dm, const std::vector<int>& utt, DevJob** 
   std::vector<int> pt((size_t)J->P * R);
   for (int i = 0; i < J->P; i++)
     for (int r = 0; r < R; r++) pt[(size_t)i * R + r] = J->prompt[i];
-  if (cudaMemcpyAsync(j->ptok, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice, j->st) != cudaSuccess ||
+  if (cudaMemcpyAsync(utt_id, j->utt.data(), (size_t)U * 4, cudaMemcpyHostToDevice, j->st) != cudaSuccess ||
+      cudaMemcpyAsync(j->ptok, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice, j->st) != cudaSuccess ||
       cudaMemcpyAsync(j->prompt_dev, J->prompt.data(), (size_t)J->P * 4, cudaMemcpyHostToDevice, j->st) !=
           cudaSuccess) {
     set_error("job setup: prompt copy failed");
@@ -642,6 +650,12 @@ int wg_model_destroy(wg_model* m) {
   return WG_OK;
 }
 
+int wg_model_set_eot(wg_model* m, int eot) {
+  if (!m) { set_error("wg_model_set_eot: null model"); return WG_ERR_INVALID; }
+  m->eot = eot;
+  return WG_OK;
+}
+
 int wg_model_weight_bytes(const wg_model* m, int64_t* bytes) {
   if (!m || !bytes || m->devs.empty()) return WG_ERR_INVALID;
   *bytes = m->devs[0]->weight_bytes;
@@ -663,10 +677,6 @@ int wg_job_create(wg_model* m, int U, int T_enc, const int32_t* prompt, int P, c
   if (params->mode != WG_MODE_REF_COMPAT && params->mode != WG_MODE_CORRECT) {
     set_error("wg_job_create: unknown mode %d", params->mode);
     return WG_ERR_INVALID;
-  }
-  if (params->logprob_thold > 0 && !params->no_fallback) {
-    set_error("model: decode: sample: the top-p fallback (LogprobThold > 0) is not implemented on the device");
-    return WG_ERR_UNSUPPORTED;
   }
   int B = params->beam_size > 1 ? params->beam_size : 1;
   if (B > 16) { set_error("model: decode: beam size %d > 16 is not supported", B); return WG_ERR_UNSUPPORTED; }
@@ -709,6 +719,64 @@ int wg_job_upload_encoder(wg_job* J, const float* const* enc) {
     WG_CHECK(wait_stream(j->st));
   }
   return WG_OK;
+}
+
+int wg_job_utterance_device(const wg_job* J, int u, int* device) {
+  if (!J || !device || u < 0 || u >= J->U) { set_error("wg_job_utterance_device: bad argument"); return WG_ERR_INVALID; }
+  for (const DevJob* j : J->dj)
+    for (int v : j->utt)
+      if (v == u) {
+        *device = j->dev;
+        return WG_OK;
+      }
+  set_error("wg_job_utterance_device: utterance %d has no device", u);
+  return WG_ERR_INVALID;
+}
+
+int wg_job_upload_encoder_device(wg_job* J, const float* const* enc, void* stream) {
+  if (!J || !enc) { set_error("wg_job_upload_encoder_device: null argument"); return WG_ERR_INVALID; }
+  const size_t per = (size_t)J->T * J->m->d;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  int prev = -1;
+  WG_CHECK_CUDA(cudaGetDevice(&prev));
+  int rc = WG_OK;
+  for (DevJob* j : J->dj) {
+    if ((rc = cudaSetDevice(j->dev) == cudaSuccess ? WG_OK : WG_ERR_CUDA) != WG_OK) break;
+    for (size_t i = 0; i < j->utt.size() && rc == WG_OK; i++) {
+      const float* src = enc[j->utt[i]];
+      cudaPointerAttributes pa;
+      if (!src || cudaPointerGetAttributes(&pa, src) != cudaSuccess || pa.type != cudaMemoryTypeDevice ||
+          pa.device != j->dev) {
+        cudaGetLastError();
+        set_error("wg_job_upload_encoder_device: utterance %d must be device memory on device %d", j->utt[i],
+                  j->dev);
+        rc = WG_ERR_INVALID;
+      }
+    }
+    if (rc != WG_OK) break;
+    // the job's stream waits for the encoder's stream (its last writes of
+    // the encoder outputs), then copies them device to device
+    cudaEvent_t ev = nullptr;
+    if (cs) {
+      if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess || cudaEventRecord(ev, cs) != cudaSuccess ||
+          cudaStreamWaitEvent(j->st, ev, 0) != cudaSuccess) {
+        set_error("wg_job_upload_encoder_device: stream ordering failed: %s", cudaGetErrorString(cudaGetLastError()));
+        rc = WG_ERR_CUDA;
+      }
+    } else if (cudaStreamSynchronize(nullptr) != cudaSuccess) {  // legacy default stream
+      set_error("wg_job_upload_encoder_device: default stream failed");
+      rc = WG_ERR_CUDA;
+    }
+    for (size_t i = 0; i < j->utt.size() && rc == WG_OK; i++)
+      if (cudaMemcpyAsync(j->enc32 + i * per, enc[j->utt[i]], per * 4, cudaMemcpyDeviceToDevice, j->st) !=
+          cudaSuccess) {
+        set_error("wg_job_upload_encoder_device: copy failed");
+        rc = WG_ERR_CUDA;
+      }
+    if (ev) cudaEventDestroy(ev);
+  }
+  cudaSetDevice(prev);
+  return rc;
 }
 
 int wg_job_start(wg_job* J) {
@@ -799,6 +867,32 @@ int wg_job_result(wg_job* J, int32_t* tokens, int32_t* lens, float* scores) {
       lens[u] = n;
       if (scores) scores[u] = J->B > 1 ? sc[row] : 0.f;
     }
+  }
+  return WG_OK;
+}
+
+int wg_job_beams(wg_job* J, int32_t* tokens, int32_t* lens, float* scores) {
+  if (!J || !tokens || !lens) { set_error("wg_job_beams: null argument"); return WG_ERR_INVALID; }
+  const int stride = J->P + J->max_tokens;
+  for (DevJob* j : J->dj) {
+    WG_CHECK_CUDA(cudaSetDevice(j->dev));
+    std::vector<int> hist((size_t)j->R * j->Tcap), len(j->R);
+    std::vector<float> sc(j->R);
+    WG_CHECK_CUDA(cudaMemcpyAsync(hist.data(), j->ss.hist, hist.size() * 4, cudaMemcpyDeviceToHost, j->st));
+    WG_CHECK_CUDA(cudaMemcpyAsync(len.data(), j->ss.len, (size_t)j->R * 4, cudaMemcpyDeviceToHost, j->st));
+    WG_CHECK_CUDA(cudaMemcpyAsync(sc.data(), j->ss.score, (size_t)j->R * 4, cudaMemcpyDeviceToHost, j->st));
+    WG_CHECK(wait_stream(j->st));
+    for (size_t i = 0; i < j->utt.size(); i++)
+      for (int b = 0; b < J->B; b++) {
+        const int u = j->utt[i], row = (int)i * J->B + b;
+        const size_t o = (size_t)u * J->B + b;
+        const int n = std::min(len[row], stride);
+        int32_t* dst = tokens + o * stride;
+        memset(dst, 0, (size_t)stride * 4);
+        memcpy(dst, hist.data() + (size_t)row * j->Tcap, (size_t)n * 4);
+        lens[o] = n;
+        if (scores) scores[o] = sc[row];
+      }
   }
   return WG_OK;
 }
@@ -1019,6 +1113,22 @@ int wg_matmul_test(uint32_t qtype, const void* raw, int rows, int cols, const fl
   free_dmat(dm);
   cudaStreamDestroy(st);
   return rc;
+}
+
+int wg_sample_test(const float* logits, int R, int V, const int32_t* hist, int n_hist, int eot,
+                   const wg_decode_params* params, int step, int32_t* out_tok, float* out_lp) {
+  if (!logits || R <= 0 || V <= 0 || n_hist < 0 || (n_hist > 0 && !hist) || !params || !out_tok || step < 0) {
+    set_error("wg_sample_test: bad argument");
+    return WG_ERR_INVALID;
+  }
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+    cudaGetLastError();
+    set_error("no CUDA device is available");
+    return WG_ERR_NO_DEVICE;
+  }
+  WG_CHECK_CUDA(cudaSetDevice(0));
+  return sample_test(logits, R, V, hist, n_hist, eot, params, step, out_tok, out_lp);
 }
 
 int wg_job_time_kernel(wg_job* J, int kclass, int iters, double* ms, double* bytes) {

@@ -244,6 +244,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int S = L.stages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* const errw = e.err_word ? e.err_word : &g_tc_error;
+  const uint64_t wait_ns = e.test_wait_ns ? e.test_wait_ns : WAIT_NS;
   const int tile0 = blockIdx.x * 8;
   const int r0 = blockIdx.y * NR;
   const int nk_all = W.cols / TC_BK;
@@ -341,7 +342,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (lane < TC_LOAD_LANES && kl < nk) {
         const int s = kl % TC_DQ_NS;
         const uint32_t ph = (uint32_t)(kl / TC_DQ_NS) & 1u;
-        ok = mbar_wait(RAW_EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 1, errw);
+        ok = mbar_wait(RAW_EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 1, errw, wait_ns);
         if (ok) issue_weights(kl);
       }
       if (!__all_sync(0xffffffffu, ok)) break;
@@ -356,8 +357,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (lane < lanes && kl < nk) {
         const int s = kl % S;
         const uint32_t ph = (uint32_t)(kl / S) & 1u;
-        ok = mbar_wait(EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 2, errw);
-        if (ok) {
+        ok = mbar_wait(EMPTY(s), ph ^ 1u, abort_flag, (kl << 8) | 2, errw, wait_ns);
+        if (ok && !(e.test_stall && kl == 0)) {
           mbar_arrive_tx(FULL(s), L.b_bytes);
           tma_2d(base + L.b0 + s * L.b_bytes, &xmap, kstage(kl) * TC_BK, r0, FULL(s));
           issued_x[s] = kl;
@@ -374,7 +375,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                              | ((uint32_t)(TC_BM >> 4) << 24);  // M
       for (int kl = 0; kl < nk; kl++) {
         const int s = kl % S;
-        if (!mbar_wait(FULL(s), (uint32_t)(kl / S) & 1u, abort_flag, (kl << 8) | 3, errw)) break;
+        if (!mbar_wait(FULL(s), (uint32_t)(kl / S) & 1u, abort_flag, (kl << 8) | 3, errw, wait_ns)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t at = tmem + TC_A_COL + 32u * (uint32_t)s;  // A in tensor memory
         const uint64_t bd = sw128_desc(base + L.b0 + s * L.b_bytes);
@@ -412,7 +413,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t ph = (uint32_t)(kl / S) & 1u;
       const int rs = kl % TC_DQ_NS;
       bool ok = mbar_wait2(RAW_FULL(rs), (uint32_t)(kl / TC_DQ_NS) & 1u, EMPTY(s), ph ^ 1u, abort_flag,
-                           (kl << 8) | 4, errw);
+                           (kl << 8) | 4, errw, wait_ns);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       const uint32_t ro = rs * L.raw_bytes;
@@ -518,7 +519,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                        : reinterpret_cast<float*>(sm);
   bool done_ok = true;
   if (warp < TC_DQ_WARPS) {
-    done_ok = mbar_wait(DONE, 0, abort_flag, 6, errw);
+    done_ok = mbar_wait(DONE, 0, abort_flag, 6, errw, wait_ns);
     done_ok = __all_sync(0xffffffffu, done_ok);
   }
   if (warp < TC_DQ_WARPS && done_ok) {
@@ -695,7 +696,14 @@ int launch_tc_t(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cu
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  cudaError_t err = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<QT>, W, map, R, NR, ks, e);
+  Epi et = e;
+  {  // failure-handling test hooks (unset in normal runs)
+    const char* v = getenv("WG_TEST_WAIT_NS");
+    et.test_wait_ns = (v && *v) ? strtoull(v, nullptr, 10) : 0;
+    v = getenv("WG_TEST_TC_STALL");
+    et.test_stall = (v && v[0] == '1') ? 1 : 0;
+  }
+  cudaError_t err = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<QT>, W, map, R, NR, ks, et);
   if (err != cudaSuccess) {
     set_error("launch of gemm_tc failed: %s", cudaGetErrorString(err));
     return WG_ERR_CUDA;

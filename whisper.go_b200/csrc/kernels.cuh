@@ -43,6 +43,13 @@ struct Epi {
   // tcgen05 path: the word an expired bounded wait records its code in
   // (device memory; nullptr: the tcgen05 kernels' shared word, tc_error_word)
   int* err_word = nullptr;
+  // tcgen05 path, set by its launcher from the environment for the
+  // failure-handling tests only: WG_TEST_WAIT_NS bounds every wait of the
+  // kernel (0: the default 2 s); WG_TEST_TC_STALL=1 makes the activation
+  // loader leave its first stage's copy out, so the MMA issuer's wait for it
+  // can only expire (the flag that nothing sets) and the abort path runs.
+  uint64_t test_wait_ns = 0;
+  int test_stall = 0;
   // Small-batch path only (matmul_fuses_input_ln): the activations are
   // LayerNorm(ln_x) of ln_d-wide fp32 rows, normalised inside the GEMV with
   // the LayerNorm kernel's arithmetic (X is not read).
@@ -147,6 +154,13 @@ struct SampleState {
   int* carried;            // [R]
   const int* forced;       // teacher forcing: [n][R] tokens or nullptr
   int* step;               // device scalar: steps taken
+  // top-p fallback of greedy steps (decoder.go:1036-1056): enabled when
+  // LogprobThold > 0, !NoFallback and the temperature is > 0; the greedy
+  // kernels then leave their pick in new_tok and topp_kernel decides
+  int topp;
+  float logprob_thold;
+  uint64_t seed;           // draws wg_uniform(seed, utt_id[u], utt_steps[u])
+  const int* utt_id;       // [U] the job's utterance index of each local utterance
 };
 // One token step of sampling: penalty, greedy argmax or beam top-5 + merge,
 // history/KV-table reorder, pos += 1.
@@ -155,6 +169,9 @@ int launch_sample_step(const SampleState& s, cudaStream_t st);
 int launch_forced_step(const SampleState& s, cudaStream_t st);
 // pos += 1 (prompt prefill passes).
 int launch_pos_inc(const SampleState& s, cudaStream_t st);
+// Kernel-level test of the token selection (wg_sample_test).
+int sample_test(const float* logits, int R, int V, const int32_t* hist, int n_hist, int eot,
+                const wg_decode_params* p, int step, int32_t* out_tok, float* out_lp);
 // Reset of the per-job state before a decode.
 int launch_sample_reset(const SampleState& s, const int* prompt_dev, cudaStream_t st);
 

@@ -11,6 +11,8 @@
 //                      table of every beam follows its parent (CORRECT mode)
 #include <cooperative_groups.h>
 
+#include <vector>
+
 #include "kernels.cuh"
 
 namespace wg {
@@ -72,6 +74,7 @@ __device__ __forceinline__ ArgMax warp_argmax(ArgMax a) {
 constexpr int SCAN_UNROLL = 8;
 
 __device__ void greedy_finish(const SampleState& s, int r, int u, ArgMax all, ArgMax excl, const float* lg);
+__device__ void greedy_commit(const SampleState& s, int r, int u, int tok);
 
 // ---- greedy ----------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) greedy_kernel(SampleState s) {
@@ -116,12 +119,19 @@ __global__ void __launch_bounds__(1024) greedy_kernel(SampleState s) {
 }
 
 // The chosen token of row r (all: arg-max of the row, excl: arg-max without
-// EOT) -> SuppressNST re-pick, history append and the stop rules (one thread).
+// EOT) -> SuppressNST re-pick, then (one thread) either the commit, or with
+// the top-p fallback enabled the pick left for topp_kernel.
 __device__ void greedy_finish(const SampleState& s, int r, int u, ArgMax all, ArgMax excl, const float* lg) {
   int tok = all.i < 0 ? 0 : all.i;
   if (s.suppress_nst && s.eot >= 0 && s.eot < s.V) {
     if (lg[s.eot] < -s.no_speech_thold && tok == s.eot) tok = excl.i < 0 ? s.eot : excl.i;
   }
+  if (s.topp) s.new_tok[r] = tok;
+  else greedy_commit(s, r, u, tok);
+}
+
+// History append, next input and the greedy loop's stop rules (decoder.go:467-484).
+__device__ void greedy_commit(const SampleState& s, int r, int u, int tok) {
   int* h = s.hist + (int64_t)r * s.Tcap;
   int n = s.len[r];
   h[n] = tok;
@@ -139,6 +149,197 @@ __device__ void greedy_finish(const SampleState& s, int r, int u, ArgMax all, Ar
     s.utt_done[u] = 1;
     atomicAdd(s.n_done, 1);
   }
+}
+
+// ---- top-p fallback of greedy steps --------------------------------------------------
+// sampleGreedyWithScratch's fallback (decoder.go:1036-1056) and
+// sampleTopPFromLogitsWithScratch (:1251-1378), one CTA per row:
+//  (1) scaled = logit / T; logZ = log(sum exp(scaled - max)) + max (float32
+//      sum of float64 exponentials); the greedy pick stands unless its
+//      log-prob is below -LogprobThold;
+//  (2) else p_i = exp(scaled_i - logZ) (float64 exponential rounded to
+//      float32, as the reference), written over the row; the nucleus is the
+//      shortest prefix of the row in descending p (lower index first among
+//      equal p) whose mass reaches 0.9, cumSum its mass, and the token is the
+//      first element of that order whose running mass reaches u01 * cumSum.
+// Both cuts are found without sorting: a radix descent over the 32-bit
+// patterns of p (non-negative floats order like their bits), 8 bits per pass,
+// with per-digit counts and masses. Masses are fixed point in units of 2^-40
+// (exact integer sums, so the result does not depend on summation order);
+// the reference sums float32 in sorted order, which differs by rounding only.
+constexpr int TOPP_THREADS = 1024;
+constexpr double TOPP_ONE = 1099511627776.0;  // 2^40
+
+__device__ __forceinline__ float uniform_dev(uint64_t seed, uint32_t u, uint32_t t) {
+  // wg_uniform (include/wg_decoder.h): SplitMix64 output function, top 24 bits
+  uint64_t z = seed ^ ((uint64_t)u + 1) * 0x9E3779B97F4A7C15ull ^ ((uint64_t)t + 1) * 0xD1B54A32D192ED03ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (float)(z >> 40) * (1.0f / 16777216.0f);
+}
+__device__ __forceinline__ unsigned long long topp_fixed(float p) { return __double2ull_rn((double)p * TOPP_ONE); }
+
+struct ToppCut {
+  uint32_t key;             // bit pattern of p at the cut
+  unsigned long long above; // mass of the elements with larger p
+  int j;                    // the cut is the j-th (1-based) element with that p, in index order
+};
+
+// Cut of row p (n floats >= 0) at cumulative mass `target` (<= the row's
+// mass): the first element, in descending p / ascending index order, whose
+// running mass reaches target. Every thread of the CTA calls it and gets it.
+__device__ ToppCut topp_cut(const float* p, int n, unsigned long long target) {
+  __shared__ unsigned int hc[256];
+  __shared__ unsigned long long hs[256];
+  __shared__ uint32_t prefix_sh, mask_sh;
+  __shared__ unsigned long long above_sh;
+  __shared__ int eq_sh;
+  if (threadIdx.x == 0) { prefix_sh = 0; mask_sh = 0; above_sh = 0; eq_sh = 0; }
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) { hc[i] = 0; hs[i] = 0; }
+    __syncthreads();
+    const uint32_t prefix = prefix_sh, mask = mask_sh;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const float v = p[i];
+      const uint32_t key = __float_as_uint(v);
+      if ((key & mask) == prefix) {
+        const int dg = (key >> shift) & 255;
+        atomicAdd(&hc[dg], 1u);
+        atomicAdd(&hs[dg], topp_fixed(v));
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long above = above_sh;
+      int sel = -1;
+      for (int dg = 255; dg >= 0; dg--) {
+        if (!hc[dg]) continue;
+        if (above + hs[dg] >= target) { sel = dg; break; }
+        above += hs[dg];
+      }
+      if (sel < 0)  // only by rounding of target: the cut is the row's last element
+        for (int dg = 0; dg < 256; dg++)
+          if (hc[dg]) { sel = dg; above -= hs[dg]; break; }
+      above_sh = above;
+      prefix_sh = prefix | ((uint32_t)sel << shift);
+      mask_sh = mask | (255u << shift);
+      eq_sh = (int)hc[sel];
+    }
+    __syncthreads();
+  }
+  ToppCut c;
+  c.key = prefix_sh;
+  c.above = above_sh;
+  const unsigned long long q = topp_fixed(__uint_as_float(c.key));
+  const unsigned long long need = target > c.above ? target - c.above : 0;
+  long long j = q ? (long long)((need + q - 1) / q) : 1;
+  if (j < 1) j = 1;
+  if (j > eq_sh) j = eq_sh;
+  c.j = (int)j;
+  __syncthreads();
+  return c;
+}
+
+// Index of the j-th (1-based) element of p whose bit pattern is key (index order).
+__device__ int topp_nth(const float* p, int n, uint32_t key, int j) {
+  __shared__ int cnt[TOPP_THREADS];
+  __shared__ int found;
+  const int chunk = (n + blockDim.x - 1) / blockDim.x;
+  const int beg = threadIdx.x * chunk, end = min(n, beg + chunk);
+  int c = 0;
+  for (int i = beg; i < end; i++) c += __float_as_uint(p[i]) == key;
+  cnt[threadIdx.x] = c;
+  if (threadIdx.x == 0) found = -1;
+  __syncthreads();
+  if (threadIdx.x == 0) {  // exclusive scan (one thread: 1024 entries)
+    int acc = 0;
+    for (int t = 0; t < (int)blockDim.x; t++) { const int v = cnt[t]; cnt[t] = acc; acc += v; }
+  }
+  __syncthreads();
+  const int before = cnt[threadIdx.x];
+  if (c > 0 && before < j && j <= before + c) {
+    int k = before;
+    for (int i = beg; i < end; i++)
+      if (__float_as_uint(p[i]) == key && ++k == j) { found = i; break; }
+  }
+  __syncthreads();
+  return found;
+}
+
+__global__ void __launch_bounds__(TOPP_THREADS) topp_kernel(SampleState s) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.x, u = r;  // greedy: B == 1
+  if (s.utt_done[u]) return;
+  float* lg = s.logits + (int64_t)r * s.V;
+  const int pick = s.new_tok[r];
+  __shared__ float red[32];
+  __shared__ unsigned long long redq[32];
+  __shared__ int fb_sh, tok_sh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  // (1) max and log Z of the scaled row
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < s.V; i += blockDim.x) mx = fmaxf(mx, __fmul_rn(lg[i], s.inv_temp));
+  mx = warp_max(mx);
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  if (warp == 0) {
+    float m = lane < nw ? red[lane] : -INFINITY;
+    m = warp_max(m);
+    if (lane == 0) red[0] = m;
+  }
+  __syncthreads();
+  mx = red[0];
+  __syncthreads();
+  float es = 0.f;
+  for (int i = threadIdx.x; i < s.V; i += blockDim.x)
+    es += (float)exp((double)__fsub_rn(__fmul_rn(lg[i], s.inv_temp), mx));
+  es = warp_sum(es);
+  if (lane == 0) red[warp] = es;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int w = 0; w < nw; w++) tot += red[w];
+    const float logZ = __fadd_rn((float)log((double)tot), mx);
+    red[0] = logZ;
+    fb_sh = __fsub_rn(__fmul_rn(lg[pick], s.inv_temp), logZ) < -s.logprob_thold;
+    tok_sh = pick;
+  }
+  __syncthreads();
+  if (fb_sh) {
+    const float logZ = red[0];
+    // (2) probabilities over the row, and its fixed-point mass
+    unsigned long long tq = 0;
+    for (int i = threadIdx.x; i < s.V; i += blockDim.x) {
+      const float p = (float)exp((double)__fsub_rn(__fmul_rn(lg[i], s.inv_temp), logZ));
+      lg[i] = p;
+      tq += topp_fixed(p);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) tq += __shfl_xor_sync(0xffffffffu, tq, o);
+    if (lane == 0) redq[warp] = tq;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long t = 0;
+      for (int w = 0; w < nw; w++) t += redq[w];
+      redq[0] = t;
+    }
+    __syncthreads();
+    const unsigned long long total = redq[0];
+    unsigned long long t1 = __double2ull_rn((double)0.9f * TOPP_ONE);  // topP = 0.9 (float32), :1037
+    if (t1 > total) t1 = total;
+    const ToppCut c1 = topp_cut(lg, s.V, t1);
+    const unsigned long long cum = c1.above + (unsigned long long)c1.j * topp_fixed(__uint_as_float(c1.key));
+    const float u01 = uniform_dev(s.seed, (uint32_t)s.utt_id[u], (uint32_t)s.utt_steps[u]);
+    unsigned long long t2 = (unsigned long long)ceil((double)u01 * (double)cum);
+    if (t2 > cum) t2 = cum;
+    const ToppCut c2 = topp_cut(lg, s.V, t2);
+    const int tok = topp_nth(lg, s.V, c2.key, c2.j);
+    if (threadIdx.x == 0 && tok >= 0) tok_sh = tok;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) greedy_commit(s, r, u, tok_sh);
 }
 
 // ---- beam: per-row top-5 of log_softmax(logits / T) ----------------------------
@@ -723,6 +924,7 @@ int launch_sample_step(const SampleState& s, cudaStream_t st) {
   if (s.B <= 1) {
     if (split) WG_CHECK(launch_check(launch_split(greedy_split_kernel, s.R, st, s), "greedy_split"));
     else WG_CHECK(launch_check(launch_k(greedy_kernel, dim3(s.R), dim3(1024), 0, st, s), "greedy"));
+    if (s.topp) WG_CHECK(launch_check(launch_k(topp_kernel, dim3(s.R), dim3(TOPP_THREADS), 0, st, s), "topp"));
   } else {
     if (split) WG_CHECK(launch_check(launch_split(topk_split_kernel, s.R, st, s), "topk_split"));
     else WG_CHECK(launch_check(launch_k(topk_kernel, dim3(s.R), dim3(TOPK_THREADS), 0, st, s), "topk"));
@@ -735,6 +937,99 @@ int launch_sample_step(const SampleState& s, cudaStream_t st) {
 int launch_forced_step(const SampleState& s, cudaStream_t st) {
   WG_CHECK(launch_check(launch_k(forced_kernel, dim3((s.R + 127) / 128), dim3(128), 0, st, s), "forced"));
   return launch_check(launch_k(pos_inc_kernel, dim3(1), dim3(1), 0, st, s.pos, s.step), "pos_inc");
+}
+
+// Kernel-level sampling test (wg_sample_test): the token-selection kernels
+// of one step on given logits, with each row its own utterance.
+int sample_test(const float* logits, int R, int V, const int32_t* hist, int n_hist, int eot,
+                const wg_decode_params* p, int step, int32_t* out_tok, float* out_lp) {
+  const bool beam = p->beam_size > 1;
+  const int Tcap = n_hist + 2;
+  cudaStream_t st = nullptr;
+  WG_CHECK_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  float *d_lg = nullptr, *d_f = nullptr;
+  int* d_i = nullptr;
+  const size_t n_i = (size_t)R * Tcap + (size_t)R * 12 + 8;
+  int rc = WG_OK;
+  if (cudaMalloc(&d_lg, (size_t)R * V * 4) != cudaSuccess || cudaMalloc(&d_f, (size_t)R * 8 * 4) != cudaSuccess ||
+      cudaMalloc(&d_i, n_i * 4) != cudaSuccess) {
+    set_error("wg_sample_test: cudaMalloc failed");
+    rc = WG_ERR_OOM;
+  }
+  SampleState s{};
+  if (rc == WG_OK) {
+    s.R = R; s.B = 1; s.U = R; s.V = V; s.eot = eot; s.Tcap = Tcap; s.P = n_hist; s.max_tokens = 1 << 20;
+    s.Tmax = 1;
+    const float base = p->temperature == 0.f ? 1.0f : p->temperature;
+    const float temp = base + (float)p->attempt * 0.2f;
+    s.inv_temp = temp > 0.f ? 1.0f / temp : 1.0f;
+    s.suppress_nst = p->suppress_nst;
+    s.no_speech_thold = p->no_speech_thold;
+    s.suppress_eot = p->suppress_eot;
+    s.topp = !beam && p->logprob_thold > 0.f && !p->no_fallback && temp > 0.f;
+    s.logprob_thold = p->logprob_thold;
+    s.seed = p->seed;
+    int* ip = d_i;
+    s.hist = ip; ip += (size_t)R * Tcap;
+    s.len = ip; ip += R;
+    s.tok_in = ip; ip += R;
+    s.new_tok = ip; ip += R;
+    s.utt_done = ip; ip += R;
+    s.utt_steps = ip; ip += R;
+    int* uid = ip; ip += R;
+    s.utt_id = uid;
+    s.topk_tok = ip; ip += (size_t)R * 5;
+    s.n_done = ip; ip += 1;
+    s.logits = d_lg;
+    s.topk_lp = d_f;
+    std::vector<int> h((size_t)R * Tcap, 0), ln(R, n_hist), z(R, 0), stp(R, step), ids(R);
+    for (int r = 0; r < R; r++) {
+      ids[r] = r;
+      for (int i = 0; i < n_hist; i++) h[(size_t)r * Tcap + i] = hist[(size_t)r * n_hist + i];
+    }
+    if (cudaMemcpyAsync(d_lg, logits, (size_t)R * V * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(s.hist, h.data(), h.size() * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(s.len, ln.data(), (size_t)R * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(s.utt_done, z.data(), (size_t)R * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(s.utt_steps, stp.data(), (size_t)R * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(uid, ids.data(), (size_t)R * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemsetAsync(s.n_done, 0, 4, st) != cudaSuccess) {
+      set_error("wg_sample_test: copy failed");
+      rc = WG_ERR_CUDA;
+    }
+  }
+  if (rc == WG_OK) {
+    const bool split = R <= sample_split_rows();
+    if (!beam) {
+      rc = split ? launch_check(launch_split(greedy_split_kernel, R, st, s), "greedy_split")
+                 : launch_check(launch_k(greedy_kernel, dim3(R), dim3(1024), 0, st, s), "greedy");
+      if (rc == WG_OK && s.topp) rc = launch_check(launch_k(topp_kernel, dim3(R), dim3(TOPP_THREADS), 0, st, s), "topp");
+    } else {
+      rc = split ? launch_check(launch_split(topk_split_kernel, R, st, s), "topk_split")
+                 : launch_check(launch_k(topk_kernel, dim3(R), dim3(TOPK_THREADS), 0, st, s), "topk");
+    }
+  }
+  if (rc == WG_OK) {
+    cudaError_t e;
+    if (!beam) {
+      std::vector<int> h((size_t)R * Tcap);
+      e = cudaMemcpyAsync(h.data(), s.hist, h.size() * 4, cudaMemcpyDeviceToHost, st);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+      for (int r = 0; r < R && e == cudaSuccess; r++) out_tok[r] = h[(size_t)r * Tcap + n_hist];
+    } else {
+      e = cudaMemcpyAsync(out_tok, s.topk_tok, (size_t)R * 5 * 4, cudaMemcpyDeviceToHost, st);
+      if (e == cudaSuccess && out_lp) e = cudaMemcpyAsync(out_lp, s.topk_lp, (size_t)R * 5 * 4, cudaMemcpyDeviceToHost, st);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    }
+    if (e != cudaSuccess) {
+      set_error("wg_sample_test: %s", cudaGetErrorString(e));
+      rc = WG_ERR_CUDA;
+    }
+  }
+  cudaStreamSynchronize(st);
+  cudaFree(d_lg); cudaFree(d_f); cudaFree(d_i);
+  cudaStreamDestroy(st);
+  return rc;
 }
 
 int launch_pos_inc(const SampleState& s, cudaStream_t st) {

@@ -81,7 +81,7 @@ class WgDecodeParams(ctypes.Structure):
         ("beam_size", ctypes.c_int32), ("temperature", ctypes.c_float), ("attempt", ctypes.c_int32),
         ("logprob_thold", ctypes.c_float), ("no_speech_thold", ctypes.c_float),
         ("no_fallback", ctypes.c_int32), ("max_tokens", ctypes.c_int32), ("suppress_nst", ctypes.c_int32),
-        ("mode", ctypes.c_int32), ("suppress_eot", ctypes.c_int32),
+        ("mode", ctypes.c_int32), ("suppress_eot", ctypes.c_int32), ("seed", ctypes.c_uint64),
     ]
 
 
@@ -100,12 +100,16 @@ def _declare(lib):
                                            ctypes.POINTER(P)]),
         "wg_model_destroy": (ctypes.c_int, [P]),
         "wg_model_weight_bytes": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_int64)]),
+        "wg_model_set_eot": (ctypes.c_int, [P, ctypes.c_int]),
         "wg_job_create": (ctypes.c_int, [P, ctypes.c_int, ctypes.c_int, c_int32_p, ctypes.c_int,
                                          ctypes.POINTER(WgDecodeParams), ctypes.POINTER(P)]),
         "wg_job_upload_encoder": (ctypes.c_int, [P, ctypes.POINTER(c_float_p)]),
+        "wg_job_upload_encoder_device": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]),
+        "wg_job_utterance_device": (ctypes.c_int, [P, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
         "wg_job_start": (ctypes.c_int, [P]),
         "wg_job_step": (ctypes.c_int, [P, ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
         "wg_job_result": (ctypes.c_int, [P, c_int32_p, c_int32_p, c_float_p]),
+        "wg_job_beams": (ctypes.c_int, [P, c_int32_p, c_int32_p, c_float_p]),
         "wg_job_cancel": (ctypes.c_int, [P]),
         "wg_job_timer": (ctypes.c_int, [P, ctypes.c_int, ctypes.POINTER(ctypes.c_double)]),
         "wg_job_destroy": (ctypes.c_int, [P]),
@@ -119,6 +123,9 @@ def _declare(lib):
         "wg_dequant_test": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_void_p, ctypes.c_int64, c_float_p]),
         "wg_matmul_test": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, c_float_p,
                                           ctypes.c_int, c_float_p, ctypes.c_int]),
+        "wg_sample_test": (ctypes.c_int, [c_float_p, ctypes.c_int, ctypes.c_int, c_int32_p, ctypes.c_int,
+                                          ctypes.c_int, ctypes.POINTER(WgDecodeParams), ctypes.c_int, c_int32_p,
+                                          c_float_p]),
         "wg_job_time_kernel": (ctypes.c_int, [P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_double),
                                               ctypes.POINTER(ctypes.c_double)]),
         "wg_model_matmul_noalloc": (ctypes.c_int, [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
@@ -255,13 +262,15 @@ class DecoderParams:
     mode: int = MODE_CORRECT
     suppress_eot: bool = False
     attempt: int = 0
+    seed: int = 0                 # top-p draws: wg_uniform(seed, utterance, step)
 
     def to_c(self) -> WgDecodeParams:
         return WgDecodeParams(beam_size=int(self.beam_size), temperature=float(self.temperature),
                               attempt=int(self.attempt), logprob_thold=float(self.logprob_thold),
                               no_speech_thold=float(self.no_speech_thold), no_fallback=int(bool(self.no_fallback)),
                               max_tokens=int(self.max_tokens), suppress_nst=int(bool(self.suppress_nst)),
-                              mode=int(self.mode), suppress_eot=int(bool(self.suppress_eot)))
+                              mode=int(self.mode), suppress_eot=int(bool(self.suppress_eot)),
+                              seed=int(self.seed) & 0xFFFFFFFFFFFFFFFF)
 
 
 def max_tokens_for(params: DecoderParams, n_text_ctx: int) -> int:
@@ -295,14 +304,68 @@ class Segment:
     speaker: int = 0
 
 
-def tokens_to_segments(tokens: Sequence[int], prompt: Sequence[int]) -> List[Segment]:
-    """internal/model/decoder.go:1415-1459 without a vocabulary."""
+def collapse_repeated_substrings(s: str, max_unit_len: int = 6, min_repeats: int = 3) -> str:
+    """internal/model/decoder.go:1188-1230 (collapseRepeatedSubstrings), on UTF-8 bytes."""
+    if not s or max_unit_len <= 0 or min_repeats <= 1:
+        return s
+    b = s.encode("utf-8")
+    n, i, out = len(b), 0, bytearray()
+    while i < n:
+        collapsed = False
+        for ln in range(1, min(max_unit_len, n - i) + 1):
+            unit = b[i:i + ln]
+            cnt, j = 1, i + ln
+            while j + ln <= n and b[j:j + ln] == unit:
+                cnt += 1
+                j += ln
+                if cnt >= min_repeats:
+                    break
+            if cnt >= min_repeats:
+                out += unit
+                i += ln * cnt
+                collapsed = True
+                break
+        if not collapsed:
+            out.append(b[i])
+            i += 1
+    return out.decode("utf-8", errors="replace")
+
+
+def compression_ratio(text: str) -> float:
+    """internal/model/decoder.go:1170-1183 (compressionRatio): byte length over
+    gzip length at the default level (6). Go's compress/flate and zlib are
+    different deflate implementations, so the compressed length can differ by
+    a few bytes from the reference's."""
+    import gzip
+    if not text:
+        return 0.0
+    raw = text.encode("utf-8")
+    comp = len(gzip.compress(raw, compresslevel=6, mtime=0))
+    return float(np.float32(len(raw)) / np.float32(comp)) if comp else float(len(raw))
+
+
+def tokens_to_segments(tokens: Sequence[int], prompt: Sequence[int], vocab=None) -> List[Segment]:
+    """internal/model/decoder.go:1415-1459: one segment of the non-prompt
+    tokens; with a vocabulary (decode_token / decode, like vocab.Vocabulary)
+    consecutive tokens with the same non-empty text are collapsed and the
+    segment text is the decoded rest with repeated substrings collapsed."""
     if len(tokens) < len(prompt):
         return []
-    rest = list(tokens[len(prompt):])
+    rest = [int(t) for t in tokens[len(prompt):]]
     if not rest:
         return []
-    return [Segment(tokens=[TokenData(id=int(t)) for t in rest])]
+    seg = Segment()
+    last, kept = "", []
+    for t in rest:
+        text = vocab.decode_token(t) if vocab is not None else ""
+        if text and text == last:
+            continue
+        last = text
+        seg.tokens.append(TokenData(id=t, text=text))
+        kept.append(t)
+    if vocab is not None:
+        seg.text = collapse_repeated_substrings(vocab.decode(kept), 6, 3)
+    return [seg]
 
 
 # ---- model descriptors ----------------------------------------------------------
@@ -413,6 +476,7 @@ class WhisperDecoder:
             nd = len(devices)
         check(lib().wg_model_create(_desc_ptr(model_desc), devs, nd, ctypes.byref(h)), "model create")
         self.h = h
+        self.vocab = None
 
     def weight_bytes(self) -> int:
         n = ctypes.c_int64()
@@ -430,25 +494,67 @@ class WhisperDecoder:
         except Exception:
             pass
 
+    def set_vocabulary(self, vocab):
+        """SetVocabulary (decoder.go:85-95): token text for the segments, the
+        compression-ratio retry, and the vocabulary's EOT id (vocab.eot >= 0)."""
+        self.vocab = vocab
+        eot = getattr(vocab, "eot", -1) if vocab is not None else -1
+        if eot is not None and eot >= 0:
+            check(lib().wg_model_set_eot(self.h, int(eot)), "set vocabulary")
+            self.eot = int(eot)
+
     # Decode (interfaces.go:22-25)
     def decode(self, encoder_out: np.ndarray, params: DecoderParams, ctx: Optional[Context] = None) -> List[Segment]:
         return self.decode_batch([encoder_out], params, ctx)[0]
 
+    ATTEMPTS = 3  # decoder.go:415, :534
+
     def decode_batch(self, encoder_outs: Sequence[np.ndarray], params: DecoderParams,
                      ctx: Optional[Context] = None) -> List[List[Segment]]:
-        toks, lens, _ = self.decode_tokens(encoder_outs, params, ctx)
-        return [tokens_to_segments(toks[u, :lens[u]], params.prompt) for u in range(len(encoder_outs))]
+        """Decode of every utterance, with the reference's retry schedule when
+        a vocabulary is set (decoder.go:433-515 greedy, :536-716 beam): an
+        utterance whose decoded text compresses by more than 2.4 is decoded
+        again at temperature + 0.2 * attempt, up to 3 attempts, unless
+        NoFallback. Retries of several utterances run as one batch."""
+        vocab = getattr(self, "vocab", None)
+        U, P = len(encoder_outs), len(params.prompt)
+        final = [None] * U
+        pending = list(range(U))
+        for attempt in range(self.ATTEMPTS if vocab is not None else 1):
+            p = dataclasses.replace(params, attempt=attempt) if vocab is not None else params
+            toks, lens, _ = self.decode_tokens([encoder_outs[u] for u in pending], p, ctx)
+            retry = []
+            for k, u in enumerate(pending):
+                final[u] = toks[k, :lens[k]]
+                gen = [int(t) for t in final[u][P:]]
+                if vocab is None or not gen:
+                    continue
+                text = vocab.decode(gen)
+                if text and compression_ratio(text) > 2.4 and attempt < self.ATTEMPTS - 1 and not params.no_fallback:
+                    retry.append(u)
+            pending = retry
+            if not pending:
+                break
+        return [tokens_to_segments(final[u], params.prompt, vocab) for u in range(U)]
 
-    def decode_tokens(self, encoder_outs, params: DecoderParams, ctx: Optional[Context] = None):
+    def decode_tokens(self, encoder_outs, params: DecoderParams, ctx: Optional[Context] = None, stream: int = 0):
+        """Tokens [U, P+max_tokens], lens [U], scores [U]. Encoder outputs are
+        host arrays, or device tensors (objects with data_ptr() and is_cuda,
+        fp32 contiguous [T, d], on the utterance's device) handed over on the
+        device after `stream` (cudaStream_t value of their producer)."""
         for e in encoder_outs:
             if e.ndim != 2 or e.shape[1] != self.n_state:
                 raise DecodeError("model: decoder: encoder output must be [T, %d], got %s" % (self.n_state,
                                                                                            list(e.shape)))
         if ctx is not None and ctx.err() is not None:
             raise DecodeError("model: decode: cancelled: context canceled", 5) from ctx.err()
+        on_device = all(getattr(e, "is_cuda", False) for e in encoder_outs)
         job = Job(self, len(encoder_outs), encoder_outs[0].shape[0], params)
         try:
-            job.upload(encoder_outs)
+            if on_device:
+                job.upload_device([e.data_ptr() for e in encoder_outs], stream)
+            else:
+                job.upload(encoder_outs)
             job.start()
             done = False
             while not done:
@@ -495,6 +601,21 @@ class Job:
         self._keep = (arrs, ptrs)
         check(lib().wg_job_upload_encoder(self.h, ptrs), "upload")
 
+    def utterance_device(self, u: int) -> int:
+        dev = ctypes.c_int(-1)
+        check(lib().wg_job_utterance_device(self.h, u, ctypes.byref(dev)))
+        return dev.value
+
+    def upload_device(self, ptrs: Sequence[int], stream: int = 0):
+        """Encoder outputs already on the GPU: ptrs[u] is the device address of
+        utterance u's [T, d] fp32 output on its device (utterance_device(u));
+        the job's stream waits for `stream` (a cudaStream_t value, 0 = legacy
+        default stream) before copying them device to device."""
+        arr = (ctypes.c_void_p * len(ptrs))(*[ctypes.c_void_p(int(p)) for p in ptrs])
+        self._keep = arr
+        check(lib().wg_job_upload_encoder_device(self.h, arr, ctypes.c_void_p(int(stream)) if stream else None),
+              "upload")
+
     def start(self):
         check(lib().wg_job_start(self.h), "start")
 
@@ -514,6 +635,17 @@ class Job:
         scores = np.zeros(self.U, dtype=np.float32)
         check(lib().wg_job_result(self.h, toks.ctypes.data_as(c_int32_p), lens.ctypes.data_as(c_int32_p),
                                   scores.ctypes.data_as(c_float_p)), "result")
+        return toks, lens, scores
+
+    def beams(self):
+        """Every hypothesis after the steps so far: tokens [U, B, P+max_tokens], lens and scores [U, B]."""
+        B = max(1, int(self.params.beam_size))
+        stride = len(self.prompt) + self.max_tokens
+        toks = np.zeros((self.U, B, stride), dtype=np.int32)
+        lens = np.zeros((self.U, B), dtype=np.int32)
+        scores = np.zeros((self.U, B), dtype=np.float32)
+        check(lib().wg_job_beams(self.h, toks.ctypes.data_as(c_int32_p), lens.ctypes.data_as(c_int32_p),
+                                 scores.ctypes.data_as(c_float_p)), "beams")
         return toks, lens, scores
 
     def stats(self):
@@ -566,6 +698,23 @@ def matmul(qtype, raw: bytes, rows: int, cols: int, x: np.ndarray, path: int = 0
     check(lib().wg_matmul_test(qt, buf.ctypes.data, rows, cols, x.ctypes.data_as(c_float_p), x.shape[0],
                                out.ctypes.data_as(c_float_p), path), "matmul")
     return out
+
+
+def sample(logits: np.ndarray, hist: np.ndarray, eot: int, params: DecoderParams, step: int = 0):
+    """The token-selection kernels of one step on given logits [R, V] and
+    histories [R, n] (wg_sample_test): greedy -> tokens [R]; beam -> (tokens
+    [R, 5], log-probs [R, 5])."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    R, V = lg.shape
+    h = np.ascontiguousarray(np.asarray(hist, dtype=np.int32).reshape(R, -1))
+    cp = params.to_c()
+    beam = params.beam_size > 1
+    tok = np.zeros(R * 5 if beam else R, dtype=np.int32)
+    lp = np.zeros(R * 5, dtype=np.float32)
+    check(lib().wg_sample_test(lg.ctypes.data_as(c_float_p), R, V, h.ctypes.data_as(c_int32_p), h.shape[1],
+                               int(eot), ctypes.byref(cp), int(step), tok.ctypes.data_as(c_int32_p),
+                               lp.ctypes.data_as(c_float_p)), "sample")
+    return (tok.reshape(R, 5), lp.reshape(R, 5)) if beam else tok
 
 
 def quantize(qtype, data: np.ndarray) -> bytes:
