@@ -154,7 +154,19 @@ int wg_kernel_launch_count(int64_t* n);
 /* Replaces model.NewDecoder (internal/model/decoder.go:97-303): uploads one
  * replica of the weights to each listed device (n_dev >= 1). */
 int wg_model_create(const wg_model_desc* desc, const int* devices, int n_dev, wg_model** out);
+/* Replaces gguf.Open + model.NewDecoder for a model file (internal/gguf/
+ * gguf.go:52-134, internal/model/decoder.go:97-303): maps the GGUF v2/v3 file
+ * read-only, resolves the decoder tensors under their whisper.cpp or
+ * Hugging Face names (internal/model/compat.go:31-148), infers the
+ * hyper-parameters the way NewDecoder does, and uploads the quantised blocks
+ * from the mapping to each listed device (no host copy; F16 vectors and
+ * transposed dense matrices are converted). EOT is 50256 until
+ * wg_model_set_eot. Errors: WG_ERR_INVALID with the reference's
+ * "gguf: ..." / "model: ..." texts. */
+int wg_model_create_from_gguf(const char* path, const int* devices, int n_dev, wg_model** out);
 int wg_model_destroy(wg_model* m);
+/* Hyper-parameters of a created model (any pointer may be NULL). */
+int wg_model_info(const wg_model* m, int* n_vocab, int* n_state, int* n_head, int* n_layer, int* n_text_ctx);
 /* The vocabulary's end-of-text id (SetVocabulary, decoder.go:85-95); jobs
  * created afterwards stop on it. */
 int wg_model_set_eot(wg_model* m, int eot);
@@ -170,6 +182,10 @@ int wg_job_create(wg_model* m, int U, int T_enc, const int32_t* prompt, int P,
 /* Host -> device copy of U encoder outputs, each [T_enc, d] fp32 row-major
  * (enc[u] points at utterance u). */
 int wg_job_upload_encoder(wg_job* j, const float* const* enc);
+/* Host -> device copy of utterance u's encoder output only (for callers,
+ * like cgo, that may pass one buffer per call but no array of pointers to
+ * their own memory); returns once the copy is done. */
+int wg_job_upload_encoder_one(wg_job* j, int u, const float* enc);
 /* Device of utterance u (the device whose memory wg_job_upload_encoder_device
  * expects its encoder output in). */
 int wg_job_utterance_device(const wg_job* j, int u, int* device);
@@ -220,6 +236,31 @@ int wg_teacher_forced_logits(wg_model* m, const float* const* enc, int U, int T_
                              const int32_t* prompt, int P,
                              const int32_t* forced, int n_forced, int mode,
                              float* logits);
+
+/* ---- pipeline batching (internal/model/pipeline.go:90-193) --------------
+ * The reference decodes one 30-s chunk per Decode call: the chunks of a file
+ * in turn, and every concurrent Transcribe (whisper.go:24) on its own
+ * goroutine. A batcher gathers such single-utterance calls into shared jobs:
+ * requests that arrive within window_us of the oldest waiting one and have
+ * the same prompt, encoder length and parameters are decoded together, up to
+ * max_utterances per job (more rows per token step for the same weight
+ * stream). One worker thread per batcher; wg_batcher_decode blocks the
+ * calling thread until its utterance is decoded and is safe to call from
+ * many threads at once. */
+typedef struct wg_batcher wg_batcher;
+int wg_batcher_create(wg_model* m, int max_utterances, int window_us, wg_batcher** out);
+/* One utterance: enc is HOST [T_enc, d] fp32 and must stay valid until the
+ * call returns; cancel (may be NULL) is polled between token steps, and a
+ * job stops early once every one of its requests is cancelled
+ * (WG_ERR_CANCELLED). tokens receives prompt + generated tokens (at most
+ * tokens_cap), *len their count, *score the beam score (0 for greedy). */
+int wg_batcher_decode(wg_batcher* b, const float* enc, int T_enc, const int32_t* prompt, int P,
+                      const wg_decode_params* params, const volatile int* cancel, int32_t* tokens, int tokens_cap,
+                      int32_t* len, float* score);
+/* Jobs run and utterances decoded so far. */
+int wg_batcher_stats(const wg_batcher* b, int64_t* jobs, int64_t* utterances);
+/* Decodes what is queued, then stops the worker. */
+int wg_batcher_destroy(wg_batcher* b);
 
 /* ---- unit entry points (kernel-level parity) ---------------------------- */
 /* Device dequantisation of raw GGUF blocks through the device weight layout

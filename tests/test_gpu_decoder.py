@@ -1,9 +1,9 @@
 """Decoder-level parity on the GPU through the C ABI against the CPU oracle.
 
 Tolerances (the north-star gate): teacher-forced logits within max-abs 2e-2
-and rel 1e-3, read as |gpu - ref| <= 2e-2 + 1e-3 * |ref| elementwise (fp32
-accumulation; f16 weight/activation operands and f16 KV caches on the
-device). Greedy tokens must be identical at every step whose oracle top-2
+and rel 1e-3 on every step, rel read as max|gpu - ref| / max|ref| (fp32
+accumulation; weights and LayerNorm outputs enter the tensor-core products
+as f16 high + low parts, f16 KV caches). Greedy tokens must be identical at every step whose oracle top-2
 margin exceeds 2e-2; comparison stops at the first step under the margin."""
 import threading
 
@@ -28,9 +28,13 @@ def tiny():
 
 
 def assert_logits_close(gpu, ref):
-    err = np.abs(gpu - ref)
-    bad = err > ATOL + RTOL * np.abs(ref)
-    assert not bad.any(), "max abs err %.3g at %s" % (err.max(), np.unravel_index(err.argmax(), err.shape))
+    """Per step: max-abs <= ATOL and max-abs <= RTOL * max|ref|."""
+    gpu, ref = np.atleast_2d(gpu), np.atleast_2d(ref)
+    for s in range(ref.shape[0]):
+        err = float(np.max(np.abs(gpu[s] - ref[s])))
+        assert err <= ATOL, "step %d: max abs err %.3g" % (s, err)
+        assert err <= RTOL * float(np.max(np.abs(ref[s]))), "step %d: max abs err %.3g > %g * max|ref|" % (
+            s, err, RTOL)
 
 
 @pytest.mark.parametrize("mode", [wgdec.MODE_REF_COMPAT, wgdec.MODE_CORRECT])
@@ -182,18 +186,32 @@ np.save({out!r}, dec.teacher_forced_logits(encs, [50258, 50259, 50357, 50363], f
 
 
 @pytest.mark.parametrize("d", [256, 384])
-def test_fused_input_layernorm_is_bit_identical(tmp_path, d):
-    """The small-batch GEMV's own LayerNorm (WG_LN_FUSE=1, the default) gives
-    exactly the logits of the separate LayerNorm kernel (WG_LN_FUSE=0), for
-    the lane-strided (d = 256) and float4 (d = 384) summation orders."""
+def test_fused_input_layernorm(tmp_path, d):
+    """The small-batch GEMV's own LayerNorm (WG_LN_FUSE=1, the default) keeps
+    the normalised activations as f16 high + low parts, the separate
+    LayerNorm kernel (WG_LN_FUSE=0) rounds them to f16 once: both meet the
+    gate, and the fused path is the closer one to the oracle (lane-strided
+    d = 256 and float4 d = 384 summation orders)."""
     import os
     import subprocess
     import sys
-    outs = []
+    outs = {}
     for fuse in ("0", "1"):
         out = tmp_path / ("logits_%s.npy" % fuse)
         code = _LN_FUSE_SCRIPT.format(pkg=str(wgdec.PKG), d=d, out=str(out))
         env = dict(os.environ, WG_LN_FUSE=fuse)
         subprocess.run([sys.executable, "-c", code], env=env, check=True, timeout=300)
-        outs.append(np.load(out))
-    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+        outs[fuse] = np.load(out)
+    m = wgdec.SyntheticModel(51864, d, d // 64, 2, 448, "Q8_0", seed=31)
+    encs = [m.encoder_output(u, 96) for u in range(2)]
+    forced = np.random.default_rng(3).integers(0, 50257, size=(2, 3))
+    errs = {}
+    for fuse, g in outs.items():
+        e = 0.0
+        for u in range(2):
+            ref = oracle.teacher_forced(m, encs[u], PROMPT, forced[u], wgdec.MODE_CORRECT, m.n_vocab)
+            assert_logits_close(g[:, u, :], ref)
+            e = max(e, float(np.sqrt(np.mean((g[:, u, :].astype(np.float64) - ref) ** 2))))
+        errs[fuse] = e
+    m.close()
+    assert errs["1"] <= errs["0"], errs

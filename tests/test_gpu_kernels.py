@@ -56,10 +56,13 @@ def _matmul_case(qt, R, rows, cols, seed):
     return raw, a, oracle.matmul(qt, raw, rows, cols, a)
 
 
-# Tolerance of the fused f16-operand / f32-accumulate kernels against the
-# oracle's f32 dot products: max |err| <= 5e-3 * rms(reference).
+# Tolerance of the fused dequant kernels (f16 tensor-core operands, fp32
+# accumulation) against the oracle's fp32 dot products: the decoder's
+# relative gate, max |err| <= 1e-3 * max |reference|. (x enters these unit
+# calls rounded to f16 once; the weights enter as f16 high + low parts on
+# the small-batch and tcgen05 paths.)
 def _close(gpu, ref):
-    return np.max(np.abs(gpu - ref)) <= 5e-3 * float(np.sqrt(np.mean(ref.astype(np.float64) ** 2)))
+    return np.max(np.abs(gpu - ref)) <= 1e-3 * float(np.max(np.abs(ref)))
 
 
 @pytest.mark.parametrize("qt", QT)

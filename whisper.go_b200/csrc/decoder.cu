@@ -650,6 +650,16 @@ int wg_model_destroy(wg_model* m) {
   return WG_OK;
 }
 
+int wg_model_info(const wg_model* m, int* n_vocab, int* n_state, int* n_head, int* n_layer, int* n_text_ctx) {
+  if (!m) { set_error("wg_model_info: null model"); return WG_ERR_INVALID; }
+  if (n_vocab) *n_vocab = m->V;
+  if (n_state) *n_state = m->d;
+  if (n_head) *n_head = m->H;
+  if (n_layer) *n_layer = m->L;
+  if (n_text_ctx) *n_text_ctx = m->ctx;
+  return WG_OK;
+}
+
 int wg_model_set_eot(wg_model* m, int eot) {
   if (!m) { set_error("wg_model_set_eot: null model"); return WG_ERR_INVALID; }
   m->eot = eot;
@@ -719,6 +729,20 @@ int wg_job_upload_encoder(wg_job* J, const float* const* enc) {
     WG_CHECK(wait_stream(j->st));
   }
   return WG_OK;
+}
+
+int wg_job_upload_encoder_one(wg_job* J, int u, const float* enc) {
+  if (!J || !enc || u < 0 || u >= J->U) { set_error("wg_job_upload_encoder_one: bad argument"); return WG_ERR_INVALID; }
+  const size_t per = (size_t)J->T * J->m->d;
+  for (DevJob* j : J->dj)
+    for (size_t i = 0; i < j->utt.size(); i++)
+      if (j->utt[i] == u) {
+        WG_CHECK_CUDA(cudaSetDevice(j->dev));
+        WG_CHECK_CUDA(cudaMemcpyAsync(j->enc32 + i * per, enc, per * 4, cudaMemcpyHostToDevice, j->st));
+        return wait_stream(j->st);  // the caller's buffer may be reused on return
+      }
+  set_error("wg_job_upload_encoder_one: utterance %d has no device", u);
+  return WG_ERR_INVALID;
 }
 
 int wg_job_utterance_device(const wg_job* J, int u, int* device) {

@@ -82,12 +82,14 @@ __device__ __forceinline__ __half2 u2h(uint32_t u) {
 // ---- epilogue (shared with gemm.cu's semantics) --------------------------------
 // Shared memory: S stages of B (activation tiles), as many as fit in 220 KB
 // next to the RAW ring (TC_DQ_NS stages of quant payloads), then the
-// mbarriers. The dequantised A tiles live in tensor memory: stage s at
-// columns TC_A_COL + 32*s (128 lanes x 64 f16), the accumulator at columns
-// 0..NR-1 (NR <= 256).
+// mbarriers. The dequantised A tiles live in tensor memory: the accumulator
+// at columns 0..NR-1 (NR <= 256), then per stage s the weight tile's f16
+// high part (128 lanes x 64 f16 = 32 columns) at tc_a_col(NR) + 64 s and its
+// low part (the f16 rounding error of the high part) 32 columns further:
+// the MMA adds both, so the weights enter the product with ~22 bits.
 constexpr int TC_S_MAX = 8;
-constexpr uint32_t TC_A_COL = 256;
 constexpr uint32_t TC_TMEM_COLS = 512;
+__host__ __device__ inline uint32_t tc_a_col(int NR) { return (uint32_t)(NR + 31) / 32 * 32; }
 struct TcLayout {
   int stages;                    // A/B ring depth
   uint32_t b_bytes;
@@ -104,6 +106,8 @@ __host__ __device__ inline TcLayout tc_layout(uint32_t qt, int NR) {
   const uint32_t raw = TC_DQ_NS * L.raw_bytes;
   L.stages = (int)((220u * 1024u - raw) / L.b_bytes);
   if (L.stages > TC_S_MAX) L.stages = TC_S_MAX;
+  const int a_stages = (int)((TC_TMEM_COLS - tc_a_col(NR)) / 64);  // hi + lo tiles per stage
+  if (L.stages > a_stages) L.stages = a_stages;
   L.b0 = 0;
   L.raw0 = L.b0 + L.stages * L.b_bytes;
   L.bar0 = L.raw0 + raw;
@@ -244,6 +248,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int S = L.stages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* const errw = e.err_word ? e.err_word : &g_tc_error;
+  const uint32_t a_col = tc_a_col(NR);
   const uint64_t wait_ns = e.test_wait_ns ? e.test_wait_ns : WAIT_NS;
   const int tile0 = blockIdx.x * 8;
   const int r0 = blockIdx.y * NR;
@@ -377,16 +382,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int s = kl % S;
         if (!mbar_wait(FULL(s), (uint32_t)(kl / S) & 1u, abort_flag, (kl << 8) | 3, errw, wait_ns)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t at = tmem + TC_A_COL + 32u * (uint32_t)s;  // A in tensor memory
+        const uint32_t at = tmem + a_col + 64u * (uint32_t)s;  // A (high, then low part) in tensor memory
         const uint64_t bd = sw128_desc(base + L.b0 + s * L.b_bytes);
 #pragma unroll
         for (int kk = 0; kk < 4; kk++) {
-          const uint32_t acc = (kl > 0 || kk > 0) ? 1u : 0u;
-          asm volatile(
-              "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-              " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem),
-              "r"(at + (uint32_t)(kk * 8)), "l"(bd + (uint64_t)(kk * 2)), "r"(idesc), "r"(acc)
-              : "memory");
+#pragma unroll
+          for (int part = 0; part < 2; part++) {
+            const uint32_t acc = (kl > 0 || kk > 0 || part > 0) ? 1u : 0u;
+            asm volatile(
+                "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem),
+                "r"(at + 32u * part + (uint32_t)(kk * 8)), "l"(bd + (uint64_t)(kk * 2)), "r"(idesc), "r"(acc)
+                : "memory");
+          }
         }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(EMPTY(s))
                      : "memory");
@@ -417,7 +425,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       const uint32_t ro = rs * L.raw_bytes;
-      uint32_t tr[16];  // the stage's 16 rows x 64 k in tcgen05.st.16x256b order
+      // the stage's 16 rows x 64 k in tcgen05.st.16x256b order: the f16 high
+      // part of every weight and its low part (the rounding error of the high
+      // part, an exact f16 FMA residual; the _1 types split d*q + m computed
+      // in float32 like the reference)
+      uint32_t tr[16], tl[16];
 #pragma unroll
       for (int blk = 0; blk < 2; blk++) {
         const __half2 dd = reinterpret_cast<const __half2*>(rd + ro)[blk * 8 + g];
@@ -438,14 +450,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (has_h) hb = reinterpret_cast<const uint16_t*>(rh + ro)[blk * 32 + lane];
 #pragma unroll
         for (int st = 0; st < 2; st++) {
-          uint32_t a[4];
+          uint32_t a[4], al[4];
+          __half2 qv[4];
           if (QT == WG_QTYPE_Q8_0) {
             uint32_t w0 = (st ? q.z : q.x) ^ 0x80808080u, w1 = (st ? q.w : q.y) ^ 0x80808080u;
             const __half2 bias = __float2half2_rn(1152.f);
-            a[0] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w0, 0x64, 0x4140)), bias), dg));
-            a[1] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w0, 0x64, 0x4342)), bias), dg8));
-            a[2] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w1, 0x64, 0x4140)), bias), dg));
-            a[3] = h2u(__hmul2(__hsub2(u2h(__byte_perm(w1, 0x64, 0x4342)), bias), dg8));
+            qv[0] = __hsub2(u2h(__byte_perm(w0, 0x64, 0x4140)), bias);
+            qv[1] = __hsub2(u2h(__byte_perm(w0, 0x64, 0x4342)), bias);
+            qv[2] = __hsub2(u2h(__byte_perm(w1, 0x64, 0x4140)), bias);
+            qv[3] = __hsub2(u2h(__byte_perm(w1, 0x64, 0x4342)), bias);
           } else {
             uint32_t w = st ? q.y : q.x;
 #pragma unroll
@@ -455,12 +468,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 uint32_t b = (hb >> (2 * (4 * st + r))) & 3u;
                 hq |= ((b & 1u) << 4) | ((b >> 1) << 20);
               }
-              const __half2 d = (r & 1) ? dg8 : dg;
-              __half2 v;
-              if (QT == WG_QTYPE_Q4_0) v = __hmul2(__hsub2(u2h(hq), __float2half2_rn(1032.f)), d);
-              else if (QT == WG_QTYPE_Q5_0) v = __hmul2(__hsub2(u2h(hq), __float2half2_rn(1040.f)), d);
-              else v = __hfma2(__hsub2(u2h(hq), __float2half2_rn(1024.f)), d, (r & 1) ? mg8 : mg);
-              a[r] = h2u(v);
+              const float off = QT == WG_QTYPE_Q4_0 ? 1032.f : (QT == WG_QTYPE_Q5_0 ? 1040.f : 1024.f);
+              qv[r] = __hsub2(u2h(hq), __float2half2_rn(off));
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < 4; r++) {
+            const __half2 d = (r & 1) ? dg8 : dg;
+            if (has_m) {
+              const float2 qf = __half22float2(qv[r]), df = __half22float2(d);
+              const float2 mf = __half22float2((r & 1) ? mg8 : mg);
+              const float v0 = __fadd_rn(__fmul_rn(df.x, qf.x), mf.x), v1 = __fadd_rn(__fmul_rn(df.y, qf.y), mf.y);
+              const __half2 hi = __floats2half2_rn(v0, v1);
+              const float2 hf = __half22float2(hi);
+              a[r] = h2u(hi);
+              al[r] = h2u(__floats2half2_rn(__fsub_rn(v0, hf.x), __fsub_rn(v1, hf.y)));
+            } else {
+              const __half2 hi = __hmul2(qv[r], d);
+              a[r] = h2u(hi);
+              al[r] = h2u(__hfma2(qv[r], d, __hneg2(hi)));
             }
           }
           // a: (row g, k 4t..4t+1), (row g+8, same k), (row g, k 4t+2..4t+3), (row g+8, ...);
@@ -470,13 +496,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tr[o + 1] = a[2];
           tr[o + 2] = a[1];
           tr[o + 3] = a[3];
+          tl[o] = al[0];
+          tl[o + 1] = al[2];
+          tl[o + 2] = al[1];
+          tl[o + 3] = al[3];
         }
       }
+      const uint32_t ta = tmem + tlane + a_col + 64u * (uint32_t)s;
       asm volatile(
           "tcgen05.st.sync.aligned.16x256b.x4.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::
-              "r"(tmem + tlane + TC_A_COL + 32u * (uint32_t)s),
+              "r"(ta),
           "r"(tr[0]), "r"(tr[1]), "r"(tr[2]), "r"(tr[3]), "r"(tr[4]), "r"(tr[5]), "r"(tr[6]), "r"(tr[7]), "r"(tr[8]),
           "r"(tr[9]), "r"(tr[10]), "r"(tr[11]), "r"(tr[12]), "r"(tr[13]), "r"(tr[14]), "r"(tr[15])
+          : "memory");
+      asm volatile(
+          "tcgen05.st.sync.aligned.16x256b.x4.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::
+              "r"(ta + 32u),
+          "r"(tl[0]), "r"(tl[1]), "r"(tl[2]), "r"(tl[3]), "r"(tl[4]), "r"(tl[5]), "r"(tl[6]), "r"(tl[7]), "r"(tl[8]),
+          "r"(tl[9]), "r"(tl[10]), "r"(tl[11]), "r"(tl[12]), "r"(tl[13]), "r"(tl[14]), "r"(tl[15])
           : "memory");
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

@@ -34,7 +34,7 @@ constexpr int GB_MAX_CLUSTER = 16;   // K ranges per group (non-portable cluster
 constexpr int GB_TARGET_CTAS = 296;  // two per SM
 
 struct GbLayout {
-  uint32_t qs, dsc, msc, hb, xs, red, stat, bar, total;
+  uint32_t qs, dsc, msc, hb, xs, xs_lo, red, stat, bar, total;
 };
 
 // Shared-memory layout for np K chunks and RC activation rows.
@@ -47,7 +47,9 @@ __host__ __device__ inline GbLayout gb_layout(uint32_t qt, int np, int RC) {
   L.hb = L.msc + (qtype_has_min(qt) ? slots * 32 : 0);
   L.xs = L.hb + (qtype_has_hbits(qt) ? slots * 64 : 0);
   const uint32_t xs_stride = (uint32_t)np * 64 + 16;  // halves; conflict-free 8-byte B-fragment loads
-  L.red = L.xs + ((uint32_t)RC * xs_stride * 2 + 15) / 16 * 16;
+  // activation rows: f16 hi, then (fused LayerNorm only) the scaled lo part
+  L.xs_lo = L.xs + ((uint32_t)RC * xs_stride * 2 + 15) / 16 * 16;
+  L.red = L.xs_lo + ((uint32_t)RC * xs_stride * 2 + 15) / 16 * 16;
   L.stat = L.red + 128u * RC * 4;  // [RC][2] LayerNorm mean, std
   L.bar = L.stat + (uint32_t)RC * 8;
   L.total = L.bar + 16;
@@ -149,6 +151,8 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
   const int k0 = p0 * 64, kn = np * 64;
   const int xs_stride = pairs_per * 64 + 16;
   __half* xsm = reinterpret_cast<__half*>(gb_smem + L.xs);
+  __half* xsm_lo = reinterpret_cast<__half*>(gb_smem + L.xs_lo);
+  const bool x_split = e.ln_x != nullptr;  // the activations have a lo part
   if (e.ln_x) {
     // fused LayerNorm: every CTA takes the statistics of the (<= 16) rows
     // and normalises its own K range, element by element as the kernel does
@@ -177,8 +181,16 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
         o[2] = __fadd_rn(__fdiv_rn(__fmul_rn(w.z, __fsub_rn(x.z, mean)), sd), b.z);
         o[3] = __fadd_rn(__fdiv_rn(__fmul_rn(w.w, __fsub_rn(x.w, mean)), sd), b.w);
       }
+      // LayerNorm output as hi + lo / 2^10 (both f16): the products keep
+      // ~22 bits of the float32 activation
       const __half2 h0 = __floats2half2_rn(o[0], o[1]), h1 = __floats2half2_rn(o[2], o[3]);
+      const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+      const __half2 l0 = __floats2half2_rn(__fmul_rn(__fsub_rn(o[0], f0.x), SPLIT_SCALE),
+                                           __fmul_rn(__fsub_rn(o[1], f0.y), SPLIT_SCALE));
+      const __half2 l1 = __floats2half2_rn(__fmul_rn(__fsub_rn(o[2], f1.x), SPLIT_SCALE),
+                                           __fmul_rn(__fsub_rn(o[3], f1.y), SPLIT_SCALE));
       *reinterpret_cast<uint2*>(xsm + rr * xs_stride + kk) = make_uint2(h2_as_u32(h0), h2_as_u32(h1));
+      *reinterpret_cast<uint2*>(xsm_lo + rr * xs_stride + kk) = make_uint2(h2_as_u32(l0), h2_as_u32(l1));
     }
   } else {
     const int cpr = kn / 8;
@@ -193,11 +205,12 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
   __syncthreads();
 
   // ---- warp w: tile w of the group over the CTA's K range ----
-  float acc[NB][4];
+  // acc: hi x hi; acl: the lo corrections (lo_w x hi_x + hi_w x lo_x), scaled by 2^10
+  float acc[NB][4], acl[NB][4];
 #pragma unroll
   for (int nb = 0; nb < NB; nb++)
 #pragma unroll
-    for (int c = 0; c < 4; c++) acc[nb][c] = 0.f;
+    for (int c = 0; c < 4; c++) acc[nb][c] = acl[nb][c] = 0.f;
   if (*abort_flag == 0) {
     const unsigned char* qsm = gb_smem + L.qs;
     const __half2* dsm = reinterpret_cast<const __half2*>(gb_smem + L.dsc);
@@ -217,13 +230,18 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
       p.hb = has_h ? hsm[slot * 32 + lane] : 0u;
 #pragma unroll
       for (int s = 0; s < 2; s++) {
-        uint32_t a[4];
-        dequant_step<QT>(p, s, a);
+        uint32_t a[4], al[4];
+        dequant_step_split<QT>(p, s, a, al);
         const int kk = kb * 32 + s * 16 + 4 * t;  // the payload's K order within 16 is the B fragment's
 #pragma unroll
         for (int nb = 0; nb < NB; nb++) {
           const uint2 bb = *reinterpret_cast<const uint2*>(xsm + (nb * 8 + g) * xs_stride + kk);
           mma16816(acc[nb], a, bb.x, bb.y);
+          mma16816(acl[nb], al, bb.x, bb.y);
+          if (x_split) {
+            const uint2 bl = *reinterpret_cast<const uint2*>(xsm_lo + (nb * 8 + g) * xs_stride + kk);
+            mma16816(acl[nb], a, bl.x, bl.y);
+          }
         }
       }
     }
@@ -234,7 +252,7 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
   for (int nb = 0; nb < NB; nb++)
 #pragma unroll
     for (int c = 0; c < 4; c++)
-      red[(warp * 16 + g + 8 * (c >> 1)) * RC + nb * 8 + 2 * t + (c & 1)] = acc[nb][c];
+      red[(warp * 16 + g + 8 * (c >> 1)) * RC + nb * 8 + 2 * t + (c & 1)] = __fmaf_rn(acl[nb][c], SPLIT_INV, acc[nb][c]);
 
   // ---- sum the cluster's K ranges in rank order, store ----
   cg::cluster_group cluster = cg::this_cluster();

@@ -104,6 +104,74 @@ __device__ __forceinline__ void dequant_step(const Pay& p, int s, uint32_t* a) {
   }
 }
 
+// Split dequantisation: the weight value v exactly as the reference
+// computes it in float32 (d*q, d*(q-8), d*(q-16), or d*q + m with two
+// float32 roundings; matmul_q8.go:237-429, dequant.go:92-201) as hi + lo / 2^10
+// with hi = f16(v) and lo = f16((v - hi) * 2^10) (scaled, so lo stays a
+// normal f16 number for |v| >= 2^-8, and hi * 2^10 stays finite for
+// |v| < 64). hi carries v to 11 bits, hi + lo/2^10 to ~22 bits, beyond the
+// float32 products' 19 significant bits for Q8_0, so the f16 tensor-core
+// products lose nothing against the reference's float32 weights.
+constexpr float SPLIT_SCALE = 1024.f, SPLIT_INV = 1.f / 1024.f;
+template <uint32_t QT>
+__device__ __forceinline__ void dequant_step_split(const Pay& p, int s, uint32_t* a, uint32_t* lo) {
+  const __half2 dg = __low2half2(p.d), dg8 = __high2half2(p.d);
+  if (QT == WG_QTYPE_Q8_0 || QT == WG_QTYPE_Q4_0 || QT == WG_QTYPE_Q5_0) {
+    // q * d is a product of two f16 values: hi = its f16 rounding (one
+    // hmul), and (q * d - hi) * 2^10 = fma(q, d * 2^10, -hi * 2^10) in f16
+    // (both scalings exact)
+    const __half2 sc = __float2half2_rn(SPLIT_SCALE);
+    const __half2 dgs = __hmul2(dg, sc), dg8s = __hmul2(dg8, sc);
+    __half2 qv[4];
+    if (QT == WG_QTYPE_Q8_0) {
+      uint32_t w0 = (s ? p.q.z : p.q.x) ^ 0x80808080u;
+      uint32_t w1 = (s ? p.q.w : p.q.y) ^ 0x80808080u;
+      const __half2 bias = __float2half2_rn(1152.f);
+      qv[0] = __hsub2(u32_as_h2(__byte_perm(w0, 0x64, 0x4140)), bias);
+      qv[1] = __hsub2(u32_as_h2(__byte_perm(w0, 0x64, 0x4342)), bias);
+      qv[2] = __hsub2(u32_as_h2(__byte_perm(w1, 0x64, 0x4140)), bias);
+      qv[3] = __hsub2(u32_as_h2(__byte_perm(w1, 0x64, 0x4342)), bias);
+    } else {
+      uint32_t w = s ? p.q.y : p.q.x;
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        uint32_t hq = ((w >> (4 * r)) & 0x000F000Fu) | 0x64006400u;
+        if (QT == WG_QTYPE_Q5_0) {
+          uint32_t b = (p.hb >> (2 * (4 * s + r))) & 3u;
+          hq |= ((b & 1u) << 4) | ((b >> 1) << 20);
+        }
+        qv[r] = __hsub2(u32_as_h2(hq), __float2half2_rn(QT == WG_QTYPE_Q4_0 ? 1032.f : 1040.f));
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const __half2 d = (r & 1) ? dg8 : dg, ds = (r & 1) ? dg8s : dgs;
+      const __half2 hi = __hmul2(qv[r], d);
+      a[r] = h2_as_u32(hi);
+      lo[r] = h2_as_u32(__hfma2(qv[r], ds, __hneg2(__hmul2(hi, sc))));
+    }
+  } else {  // Q4_1 / Q5_1: v = float32(float32(d * q) + m), then the split in float32
+    uint32_t w = s ? p.q.y : p.q.x;
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      uint32_t hq = ((w >> (4 * r)) & 0x000F000Fu) | 0x64006400u;
+      if (QT == WG_QTYPE_Q5_1) {
+        uint32_t b = (p.hb >> (2 * (4 * s + r))) & 3u;
+        hq |= ((b & 1u) << 4) | ((b >> 1) << 20);
+      }
+      const float2 q = __half22float2(__hsub2(u32_as_h2(hq), __float2half2_rn(1024.f)));
+      const float2 d = __half22float2((r & 1) ? dg8 : dg);
+      const float2 m = __half22float2((r & 1) ? __high2half2(p.m) : __low2half2(p.m));
+      const float v0 = __fadd_rn(__fmul_rn(d.x, q.x), m.x), v1 = __fadd_rn(__fmul_rn(d.y, q.y), m.y);
+      const __half2 hi = __floats2half2_rn(v0, v1);
+      const float2 h = __half22float2(hi);
+      a[r] = h2_as_u32(hi);
+      lo[r] = h2_as_u32(__floats2half2_rn(__fmul_rn(__fsub_rn(v0, h.x), SPLIT_SCALE),
+                                          __fmul_rn(__fsub_rn(v1, h.y), SPLIT_SCALE)));
+    }
+  }
+}
+
 __device__ __forceinline__ void epi_store(const Epi& e, int r, int n, float v) {
   switch (e.mode) {
     case EPI_F32:

@@ -98,6 +98,8 @@ def _declare(lib):
         "wg_kernel_launch_count": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int64)]),
         "wg_model_create": (ctypes.c_int, [ctypes.POINTER(WgModelDesc), ctypes.POINTER(ctypes.c_int), ctypes.c_int,
                                            ctypes.POINTER(P)]),
+        "wg_model_create_from_gguf": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_int), ctypes.c_int,
+                                                     ctypes.POINTER(P)]),
         "wg_model_destroy": (ctypes.c_int, [P]),
         "wg_model_weight_bytes": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_int64)]),
         "wg_model_set_eot": (ctypes.c_int, [P, ctypes.c_int]),
@@ -120,6 +122,12 @@ def _declare(lib):
         "wg_teacher_forced_logits": (ctypes.c_int, [P, ctypes.POINTER(c_float_p), ctypes.c_int, ctypes.c_int,
                                                     c_int32_p, ctypes.c_int, c_int32_p, ctypes.c_int, ctypes.c_int,
                                                     c_float_p]),
+        "wg_batcher_create": (ctypes.c_int, [P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(P)]),
+        "wg_batcher_decode": (ctypes.c_int, [P, c_float_p, ctypes.c_int, c_int32_p, ctypes.c_int,
+                                             ctypes.POINTER(WgDecodeParams), ctypes.POINTER(ctypes.c_int), c_int32_p,
+                                             ctypes.c_int, c_int32_p, c_float_p]),
+        "wg_batcher_stats": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)]),
+        "wg_batcher_destroy": (ctypes.c_int, [P]),
         "wg_dequant_test": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_void_p, ctypes.c_int64, c_float_p]),
         "wg_matmul_test": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, c_float_p,
                                           ctypes.c_int, c_float_p, ctypes.c_int]),
@@ -478,6 +486,20 @@ class WhisperDecoder:
         self.h = h
         self.vocab = None
 
+    @classmethod
+    def from_gguf(cls, path, devices: Optional[Sequence[int]] = None) -> "WhisperDecoder":
+        """NewDecoder on a GGUF model file (wg_model_create_from_gguf)."""
+        self = cls.__new__(cls)
+        self._src = None
+        h = ctypes.c_void_p()
+        devs = (ctypes.c_int * len(devices))(*devices) if devices else None
+        check(lib().wg_model_create_from_gguf(str(path).encode(), devs, len(devices) if devices else 0,
+                                              ctypes.byref(h)), "model create")
+        self.h = h
+        self.vocab = None
+        self.eot = 50256
+        return self
+
     def weight_bytes(self) -> int:
         n = ctypes.c_int64()
         check(lib().wg_model_weight_bytes(self.h, ctypes.byref(n)))
@@ -580,6 +602,54 @@ class WhisperDecoder:
                                              len(pr), fo.ctypes.data_as(c_int32_p), n, mode,
                                              out.ctypes.data_as(c_float_p)), "teacher forcing")
         return out
+
+
+class Batcher:
+    """Pipeline batching (wg_batcher_*): decode() from many threads at once;
+    compatible calls within `window_us` share one GPU job (ctypes releases
+    the GIL for the blocking call, so the threads wait in parallel)."""
+
+    def __init__(self, dec: WhisperDecoder, max_utterances: int = 64, window_us: int = 2000):
+        self.dec = dec
+        h = ctypes.c_void_p()
+        check(lib().wg_batcher_create(dec.h, max_utterances, window_us, ctypes.byref(h)), "batcher")
+        self.h = h
+
+    def decode_tokens(self, encoder_out: np.ndarray, params: DecoderParams, ctx: Optional[Context] = None):
+        """(tokens, score) of one utterance, prompt included."""
+        enc = np.ascontiguousarray(encoder_out, dtype=np.float32)
+        pr = np.asarray(params.prompt, dtype=np.int32)
+        cap = len(pr) + max_tokens_for(params, self.dec.n_text_ctx)
+        toks = np.zeros(max(cap, 1), dtype=np.int32)
+        n = ctypes.c_int32(0)
+        sc = ctypes.c_float(0)
+        cp = params.to_c()
+        flag = ctypes.c_int(0)
+        watcher = None
+        if ctx is not None:  # ctx.Done() -> the request's cancel flag
+            def watch():
+                ctx._canceled.wait()
+                flag.value = 1
+            watcher = threading.Thread(target=watch, daemon=True)
+            watcher.start()
+        check(lib().wg_batcher_decode(self.h, enc.ctypes.data_as(c_float_p), enc.shape[0], pr.ctypes.data_as(c_int32_p),
+                                      len(pr), ctypes.byref(cp), ctypes.byref(flag), toks.ctypes.data_as(c_int32_p),
+                                      len(toks), ctypes.byref(n), ctypes.byref(sc)), "batcher")
+        return toks[:n.value], sc.value
+
+    def decode(self, encoder_out: np.ndarray, params: DecoderParams, ctx: Optional[Context] = None) -> List[Segment]:
+        toks, _ = self.decode_tokens(encoder_out, params, ctx)
+        return tokens_to_segments(toks, params.prompt, getattr(self.dec, "vocab", None))
+
+    def stats(self):
+        j, u = ctypes.c_int64(), ctypes.c_int64()
+        check(lib().wg_batcher_stats(self.h, ctypes.byref(j), ctypes.byref(u)))
+        return j.value, u.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().wg_batcher_destroy(self.h)
+            self.h = None
 
 
 class Job:
