@@ -1,0 +1,732 @@
+// step.cu — the decoder's layers for one token step as ONE persistent kernel
+// (small batches: up to 16 rows per step, i.e. up to 3 utterances x beam 5).
+//
+// At batch 1 a token step of forward (internal/model/decoder.go:745-833) is a
+// chain of ~8 dependent operations per layer (LayerNorm + q|k|v matmul,
+// self-attention, output matmul, LayerNorm + cross q, cross-attention, output
+// matmul, LayerNorm + mlp.0 + GELU, mlp.2), each moving a few MB: as
+// separate kernels every one costs a launch plus a pipeline fill, ~5-7 us,
+// against ~0.2-1 us of HBM time. This kernel runs all of them for all layers
+// with one CTA per SM, the phases separated by a grid-wide barrier
+// (co-residency guaranteed by a cooperative launch; every wait bounded):
+//
+//  matmul phases: the weight matrix is cut into units of one 128-row group x
+//    a range of 64-wide K chunks (the tile128 layout makes each unit one
+//    contiguous run per plane); each CTA walks its units of the whole step
+//    in order and bulk-copies them into a two-slot shared-memory ring ahead
+//    of use (weights never depend on activations, so the copy of the next
+//    unit overlaps the current phase and the barrier). A unit multiplies its
+//    K range of the activations (LayerNorm applied on the fly where one
+//    precedes, from the fp32 residual stream) on mma.m16n8k16 with the weights
+//    and activations as f16 high + low parts, writes its fp32 partial tile,
+//    and the last unit of a group to arrive (an arrival counter) sums the
+//    group's K splits in order — deterministic — and applies the epilogue
+//    (bias, residual add, GELU, q / K / V with the K and V of this position
+//    written to the cache).
+//  self-attention: one unit per (row, head) (decoder.go:836-908).
+//  cross-attention: units of (utterance, head, frame chunk); the chunks of a
+//    head exchange their maxima through global memory (a local bounded wait)
+//    so the softmax uses the exact maximum of all 1,500 frames, like the
+//    reference; partial sums are combined by the next matmul phase when it
+//    stages its activations (decoder.go:911-971, attention.go:193-317).
+//
+// Arithmetic follows the separate kernels: LayerNorm two-pass in fp32
+// (ops.go:153-202), the reference fast exponential, exact maxima, fp32
+// accumulation.
+#include <cooperative_groups.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "async.cuh"
+#include "gemv_frag.cuh"
+
+namespace wg {
+
+__device__ int g_step_error;  // first expired wait of the step kernel: (phase << 8) | site
+
+namespace {
+
+constexpr int ST_WARPS = 8;  // one per 16-row tile of a 128-row group
+constexpr int ST_THREADS = ST_WARPS * 32;
+constexpr int ST_MAX_PAIRS = 8;  // 64-wide K chunks of one matmul unit
+constexpr int ST_MAX_ROWS = 16;
+constexpr int ST_MAX_CHUNKS = 8;  // frame chunks of one cross-attention head
+constexpr int ST_MAX_POS = 448;   // KV positions (n_text_ctx)
+constexpr int ST_MAX_FRAMES_CHUNK = 512;
+
+// Layer weights and vectors as the kernel reads them (device array).
+struct StepLayer {
+  DMat w[6];  // q|k|v, self out, cross q, cross out, mlp.0, mlp.2
+  const float *sln_w, *sln_b, *cln_w, *cln_b, *mln_w, *mln_b;
+  const float *q_b, *v_b, *so_b, *cq_b, *co_b, *m0_b, *m2_b;
+};
+
+// One matmul of the step: its K split and the units it has.
+struct MmPlan {
+  int groups, pairs, ks, per;  // 128-row groups, 64-wide K pairs, K splits, pairs per split
+};
+
+struct StepArgs {
+  const StepLayer* layers;
+  int L, R, U, B, d, H, T, Tmax;
+  MmPlan mm[6];
+  int xchunks;                 // frame chunks per cross-attention head
+  const int* pos;              // device scalar
+  const int* tbl;              // [R][Tmax] physical row of each position (beams, CORRECT) or nullptr
+  int ref_compat, zero_unless_pos0;
+  float* x;                    // [R][d] residual stream (embedding already added)
+  float* q;                    // [R][d] self-attention q, then cross-attention q
+  float* att;                  // [R][d] self-attention output
+  float* h;                    // [R][4d] GELU(mlp.0)
+  __half* selfkv;              // [L][R][2][H][Tmax][64]
+  const __half* cross;         // [L][U][2][H][T][64]
+  float* part;                 // matmul partial tiles [unit][R][128]
+  float* xpart;                // cross-attention partials [chunk][R][H][65] (o[64], l)
+  float* xmax;                 // [chunk][R][H] per-chunk maxima
+  unsigned* sync;              // [0] grid barrier, [1] exits, [2] abort, [4..4+G) group counters, then [U*H] head counters
+  int max_groups;
+  int* err;
+};
+
+// ---------------------------------------------------------------------------
+// synchronisation (all waits bounded: 2 s of %globaltimer)
+// ---------------------------------------------------------------------------
+constexpr uint64_t ST_WAIT_NS = 2000000000ull;
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ bool aborted(const StepArgs& a) { return ld_acquire(a.sync + 2) != 0; }
+__device__ void raise_abort(const StepArgs& a, int code) {
+  atomicCAS(a.err, 0, code);
+  atomicExch(a.sync + 2, 1u);
+}
+
+// Spin (thread 0 only) until *p reaches target (wrap-safe), or abort/timeout.
+__device__ bool spin_until(const StepArgs& a, const unsigned* p, unsigned target, int code) {
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0;; i++) {
+    if ((int)(ld_acquire(p) - target) >= 0) return true;
+    if (ld_acquire(a.sync + 2)) return false;
+    if ((i & 63) == 63 && global_ns() - t0 > ST_WAIT_NS) {
+      raise_abort(a, code);
+      return false;
+    }
+    __nanosleep(64);
+  }
+}
+
+// Grid-wide barrier: every CTA's writes before it are visible to every CTA after it.
+__device__ void grid_barrier(const StepArgs& a, unsigned& target, int code) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    target += gridDim.x;
+    __threadfence();
+    red_release(a.sync, 1u);
+    spin_until(a, a.sync, target, code);
+    __threadfence();
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// weight stream: the CTA's matmul units of the whole step, in order, through
+// a two-slot shared-memory ring (one bulk copy per plane per unit)
+// ---------------------------------------------------------------------------
+struct Ring {
+  uint32_t base;           // shared address of slot 0
+  uint32_t slot_bytes;
+  uint32_t bar;            // two mbarriers
+  int issued, consumed;    // units issued / consumed so far
+  int total;               // units of this CTA in the step
+};
+
+// Unit u of the CTA's sequence -> (layer, matrix, group, k split).
+struct UnitRef {
+  int l, m, g, kz;
+};
+
+__device__ __forceinline__ int units_of(const MmPlan& p) { return p.groups * p.ks; }
+// the k-th unit (k >= 0) this CTA processes in the step, or l = -1 past the end
+__device__ UnitRef unit_at(const StepArgs& a, int k) {
+  const int G = gridDim.x, b = blockIdx.x;
+  int left = k;
+  for (int l = 0; l < a.L; l++)
+    for (int m = 0; m < 6; m++) {
+      const int n = units_of(a.mm[m]);
+      const int mine = n > b ? (n - b + G - 1) / G : 0;  // units b, b+G, ...
+      if (left < mine) {
+        const int u = b + left * G;
+        return UnitRef{l, m, u / a.mm[m].ks, u % a.mm[m].ks};
+      }
+      left -= mine;
+    }
+  return UnitRef{-1, 0, 0, 0};
+}
+
+template <uint32_t QT>
+__device__ __forceinline__ uint32_t unit_bytes(int np) {
+  constexpr uint32_t pb = QT == WG_QTYPE_Q8_0 ? 16 : 8;
+  constexpr bool has_m = QT == WG_QTYPE_Q4_1 || QT == WG_QTYPE_Q5_1;
+  constexpr bool has_h = QT == WG_QTYPE_Q5_0 || QT == WG_QTYPE_Q5_1;
+  return (uint32_t)np * 16 * (32 * pb + 32 + (has_m ? 32 : 0) + (has_h ? 64 : 0));
+}
+
+// Issues unit k's copies into slot k % 2 (thread 0; the slot is free).
+template <uint32_t QT>
+__device__ void ring_issue(const StepArgs& a, Ring& rg, int k) {
+  const UnitRef ur = unit_at(a, k);
+  if (ur.l < 0) return;
+  constexpr uint32_t pb = QT == WG_QTYPE_Q8_0 ? 16 : 8;
+  constexpr bool has_m = QT == WG_QTYPE_Q4_1 || QT == WG_QTYPE_Q5_1;
+  constexpr bool has_h = QT == WG_QTYPE_Q5_0 || QT == WG_QTYPE_Q5_1;
+  const MmPlan& pl = a.mm[ur.m];
+  const DMat& W = a.layers[ur.l].w[ur.m];
+  const int p0 = ur.kz * pl.per, np = min(pl.per, pl.pairs - p0);
+  const uint32_t slots = (uint32_t)np * 16;
+  const int64_t S0 = ((int64_t)ur.g * pl.pairs + p0) * 16;
+  const uint32_t dst = rg.base + (uint32_t)(k & 1) * rg.slot_bytes, bar = rg.bar + 8 * (k & 1);
+  const uint32_t qb = slots * 32 * pb;
+  mbar_arrive_tx(bar, unit_bytes<QT>(np));
+  bulk_g2s(dst, W.qs + S0 * 32 * pb, qb, bar);
+  bulk_g2s(dst + qb, W.dsc + S0 * 8, slots * 32, bar);
+  uint32_t o = qb + slots * 32;
+  if (has_m) {
+    bulk_g2s(dst + o, W.msc + S0 * 8, slots * 32, bar);
+    o += slots * 32;
+  }
+  if (has_h) bulk_g2s(dst + o, W.hb + S0 * 32, slots * 64, bar);
+}
+
+// ---------------------------------------------------------------------------
+// activations of a matmul unit
+// ---------------------------------------------------------------------------
+// Row statistics of LayerNorm (ops.go:153-202) for all rows: mean, std.
+__device__ void ln_stats(const StepArgs& a, float* stat) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = warp; r < a.R; r += ST_WARPS) {
+    const float* xr = a.x + (int64_t)r * a.d;
+    float s = 0.f;
+    for (int i = lane; i < a.d; i += 32) s += __ldcg(xr + i);
+    s = warp_sum(s);
+    const float mean = __fdiv_rn(s, (float)a.d);
+    float q = 0.f;
+    for (int i = lane; i < a.d; i += 32) {
+      const float dd = __fsub_rn(__ldcg(xr + i), mean);
+      q = __fmaf_rn(dd, dd, q);
+    }
+    q = warp_sum(q);
+    if (lane == 0) {
+      stat[2 * r] = mean;
+      stat[2 * r + 1] = __fsqrt_rn(__fadd_rn(__fdiv_rn(q, (float)a.d), 1e-5f));
+    }
+  }
+}
+
+enum Src { SRC_LN = 0, SRC_ATT = 1, SRC_CROSS = 2, SRC_H = 3 };
+
+// Stages rows [0, RC) x columns [k0, k0 + kn) of the unit's input as f16
+// high + (scaled) low parts: x_hi = f16(v), x_lo = f16((v - x_hi) * 2^10).
+__device__ void stage_x(const StepArgs& a, int src, const float* lnw, const float* lnb, const float* stat, int k0,
+                        int kn, int RC, int stride, __half* xh, __half* xl) {
+  const int width = src == SRC_H ? 4 * a.d : a.d;
+  for (int i = threadIdx.x; i < RC * kn; i += blockDim.x) {
+    const int r = i / kn, kk = i - r * kn, k = k0 + kk;
+    float v = 0.f;
+    if (r < a.R) {
+      if (src == SRC_LN) {
+        const float xv = __ldcg(a.x + (int64_t)r * a.d + k);
+        v = __fadd_rn(__fdiv_rn(__fmul_rn(lnw[k], __fsub_rn(xv, stat[2 * r])), stat[2 * r + 1]), lnb[k]);
+      } else if (src == SRC_ATT) {
+        v = __ldcg(a.att + (int64_t)r * a.d + k);
+      } else if (src == SRC_H) {
+        v = __ldcg(a.h + (int64_t)r * width + k);
+      } else {  // cross-attention: combine the frame chunks of (row, head)
+        const int hh = k >> 6, c = k & 63;
+        float o = 0.f, l = 0.f;
+        for (int ch = 0; ch < a.xchunks; ch++) {
+          const float* p = a.xpart + (((int64_t)ch * a.R + r) * a.H + hh) * 65;
+          o += __ldcg(p + c);
+          l += __ldcg(p + 64);
+        }
+        v = __fmul_rn(o, __fdiv_rn(1.0f, l));
+      }
+    }
+    const __half hv = __float2half_rn(v);
+    xh[r * stride + kk] = hv;
+    xl[r * stride + kk] = __float2half_rn(__fmul_rn(__fsub_rn(v, __half2float(hv)), SPLIT_SCALE));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// one matmul unit: partial tile, then (last arriver of its group) the epilogue
+// ---------------------------------------------------------------------------
+template <uint32_t QT, int NB>
+__device__ void mm_unit(const StepArgs& a, const UnitRef& ur, const unsigned char* wsm, unsigned char* smem_x,
+                        float* red, const float* stat, unsigned& ok_flag) {
+  constexpr int RC = NB * 8;
+  constexpr int pb = QT == WG_QTYPE_Q8_0 ? 16 : 8;
+  constexpr bool has_m = QT == WG_QTYPE_Q4_1 || QT == WG_QTYPE_Q5_1;
+  constexpr bool has_h = QT == WG_QTYPE_Q5_0 || QT == WG_QTYPE_Q5_1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const StepLayer& ly = a.layers[ur.l];
+  const MmPlan& pl = a.mm[ur.m];
+  const int p0 = ur.kz * pl.per, np = min(pl.per, pl.pairs - p0);
+  const int k0 = p0 * 64, kn = np * 64, stride = ST_MAX_PAIRS * 64 + 16;
+  __half* xh = reinterpret_cast<__half*>(smem_x);
+  __half* xl = xh + RC * stride;
+  // input of this matmul
+  const int src = ur.m == 0 || ur.m == 2 || ur.m == 4 ? SRC_LN : (ur.m == 1 ? SRC_ATT : (ur.m == 3 ? SRC_CROSS : SRC_H));
+  const float* lnw = ur.m == 0 ? ly.sln_w : (ur.m == 2 ? ly.cln_w : ly.mln_w);
+  const float* lnb = ur.m == 0 ? ly.sln_b : (ur.m == 2 ? ly.cln_b : ly.mln_b);
+  stage_x(a, src, lnw, lnb, stat, k0, kn, RC, stride, xh, xl);
+  __syncthreads();
+  // warp w: tile w of the group (weights in the ring slot: qs | dsc | msc | hb)
+  const uint32_t slots = (uint32_t)np * 16;
+  const unsigned char* qsm = wsm;
+  const __half2* dsm = reinterpret_cast<const __half2*>(wsm + slots * 32 * pb);
+  const __half2* msm = reinterpret_cast<const __half2*>(wsm + slots * 32 * pb + slots * 32);
+  const uint16_t* hsm =
+      reinterpret_cast<const uint16_t*>(wsm + slots * 32 * pb + slots * 32 + (has_m ? slots * 32 : 0));
+  float acc[NB][4], acl[NB][4];
+#pragma unroll
+  for (int nb = 0; nb < NB; nb++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) acc[nb][c] = acl[nb][c] = 0.f;
+  for (int kb = 0; kb < 2 * np; kb++) {
+    const int slot = (kb >> 1) * 16 + warp * 2 + (kb & 1);
+    Pay p;
+    if (QT == WG_QTYPE_Q8_0) p.q = reinterpret_cast<const uint4*>(qsm)[slot * 32 + lane];
+    else {
+      const uint2 v = reinterpret_cast<const uint2*>(qsm)[slot * 32 + lane];
+      p.q = make_uint4(v.x, v.y, 0, 0);
+    }
+    p.d = dsm[slot * 8 + g];
+    p.m = has_m ? msm[slot * 8 + g] : __float2half2_rn(0.f);
+    p.hb = has_h ? hsm[slot * 32 + lane] : 0u;
+#pragma unroll
+    for (int s = 0; s < 2; s++) {
+      uint32_t aw[4], al[4];
+      dequant_step_split<QT>(p, s, aw, al);
+      const int kk = kb * 32 + s * 16 + 4 * t;
+#pragma unroll
+      for (int nb = 0; nb < NB; nb++) {
+        const uint2 bh = *reinterpret_cast<const uint2*>(xh + (nb * 8 + g) * stride + kk);
+        const uint2 bl = *reinterpret_cast<const uint2*>(xl + (nb * 8 + g) * stride + kk);
+        mma16816(acc[nb], aw, bh.x, bh.y);
+        mma16816(acl[nb], al, bh.x, bh.y);
+        mma16816(acl[nb], aw, bl.x, bl.y);
+      }
+    }
+  }
+  // partial tile [R][128] of this K split -> global
+  float* mine = a.part + ((int64_t)(ur.g * pl.ks + ur.kz)) * a.R * 128;
+#pragma unroll
+  for (int nb = 0; nb < NB; nb++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      const int row = warp * 16 + g + 8 * (c >> 1), col = nb * 8 + 2 * t + (c & 1);
+      if (col < a.R) mine[col * 128 + row] = __fmaf_rn(acl[nb][c], SPLIT_INV, acc[nb][c]);
+    }
+  __syncthreads();
+  // arrival: the last K split of the group reduces and stores
+  __shared__ int last;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    unsigned* cnt = a.sync + 4 + ur.g;
+    const unsigned old = atomicAdd(cnt, 1u);
+    last = old == (unsigned)(pl.ks - 1);
+    if (last) {
+      atomicExch(cnt, 0u);  // the next use of the counter is after a grid barrier
+      __threadfence();
+    }
+  }
+  __syncthreads();
+  if (!last) return;
+  const float* base = a.part + (int64_t)ur.g * pl.ks * a.R * 128;
+  const int N = a.layers[ur.l].w[ur.m].rows;
+  const int pos = *a.pos;
+  for (int i = threadIdx.x; i < a.R * 128; i += blockDim.x) {
+    const int r = i >> 7, row = i & 127, n = ur.g * 128 + row;
+    if (n >= N) continue;
+    float v = 0.f;
+    for (int kz = 0; kz < pl.ks; kz++) v += __ldcg(base + ((int64_t)kz * a.R + r) * 128 + row);  // in split order
+    switch (ur.m) {
+      case 0: {  // q | k | v (decoder.go:840-870); K and V of this position into the cache
+        const int seg = n / a.d, j = n - seg * a.d, hh = j >> 6, c = j & 63;
+        if (seg == 0) {
+          a.q[(int64_t)r * a.d + j] = __fadd_rn(v, ly.q_b[j]);
+        } else {
+          if (seg == 2) v = __fadd_rn(v, ly.v_b[j]);
+          __half* kv = a.selfkv + (int64_t)ur.l * a.R * 2 * a.H * a.Tmax * 64;
+          kv[((((int64_t)r * 2 + (seg - 1)) * a.H + hh) * a.Tmax + pos) * 64 + c] = __float2half_rn(v);
+        }
+        break;
+      }
+      case 1: a.x[(int64_t)r * a.d + n] = __fadd_rn(__ldcg(a.x + (int64_t)r * a.d + n), __fadd_rn(v, ly.so_b[n])); break;
+      case 2: a.q[(int64_t)r * a.d + n] = __fadd_rn(v, ly.cq_b[n]); break;
+      case 3: a.x[(int64_t)r * a.d + n] = __fadd_rn(__ldcg(a.x + (int64_t)r * a.d + n), __fadd_rn(v, ly.co_b[n])); break;
+      case 4: a.h[(int64_t)r * 4 * a.d + n] = gelu_f32(__fadd_rn(v, ly.m0_b[n])); break;
+      default: a.x[(int64_t)r * a.d + n] = __fadd_rn(__ldcg(a.x + (int64_t)r * a.d + n), __fadd_rn(v, ly.m2_b[n])); break;
+    }
+  }
+  (void)ok_flag;
+}
+
+// All of this CTA's units of matmul m of layer l.
+template <uint32_t QT, int NB>
+__device__ void mm_phase(const StepArgs& a, Ring& rg, int l, int m, unsigned char* smem_x, float* red, float* stat,
+                         unsigned char* smem, int phase_code) {
+  const MmPlan& pl = a.mm[m];
+  const int n = units_of(pl);
+  if ((int)blockIdx.x >= n) return;
+  if (m == 0 || m == 2 || m == 4) {
+    ln_stats(a, stat);
+    __syncthreads();
+  }
+  unsigned okf = 1;
+  for (int u = blockIdx.x; u < n; u += gridDim.x) {
+    const int k = rg.consumed;
+    // the unit's weights: wait for the slot's copy
+    __shared__ int wok;
+    if (threadIdx.x == 0) {
+      wok = mbar_wait(rg.bar + 8 * (k & 1), (uint32_t)(k >> 1) & 1u, reinterpret_cast<volatile int*>(a.sync + 2),
+                      (phase_code << 8) | 1, a.err);
+      if (!wok) atomicExch(a.sync + 2, 1u);
+    }
+    __syncthreads();
+    if (!wok) return;
+    const UnitRef ur{l, m, u / pl.ks, u % pl.ks};
+    mm_unit<QT, NB>(a, ur, smem + (uint32_t)(k & 1) * rg.slot_bytes, smem_x, red, stat, okf);
+    __syncthreads();  // every warp is done with the slot
+    rg.consumed++;
+    if (threadIdx.x == 0 && rg.issued < rg.total) ring_issue<QT>(a, rg, rg.issued);
+    rg.issued = min(rg.issued + 1, rg.total);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// attention phases
+// ---------------------------------------------------------------------------
+// Self-attention of (row r, head h) over positions 0..pos (decoder.go:836-908).
+__device__ void self_attn_unit(const StepArgs& a, int l, int r, int hh, float* sm) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pos = *a.pos;
+  float* out = a.att + (int64_t)r * a.d + hh * 64;
+  if (a.zero_unless_pos0 && pos != 0) {  // slot 0 was reset (decoder.go:593): output exactly 0
+    for (int c = threadIdx.x; c < 64; c += blockDim.x) out[c] = 0.f;
+    return;
+  }
+  const int n = a.ref_compat ? 1 : pos + 1;
+  float* qs = sm;               // [64]
+  float* sc = sm + 64;          // [n]
+  float* red = sc + ST_MAX_POS; // [ST_WARPS][64] + [ST_WARPS]
+  for (int c = threadIdx.x; c < 64; c += blockDim.x) qs[c] = __ldcg(a.q + (int64_t)r * a.d + hh * 64 + c);
+  __syncthreads();
+  const __half* kvl = a.selfkv + (int64_t)l * a.R * 2 * a.H * a.Tmax * 64;
+  const float scale = 0.125f;  // 1 / sqrt(64)
+  auto slab = [&](int tt) -> int64_t {
+    const int pr = a.tbl ? __ldcg(a.tbl + (int64_t)r * a.Tmax + tt) : r;
+    return (((int64_t)pr * 2) * a.H + hh) * a.Tmax;
+  };
+  // scores: one position per thread (its K row: eight 16-byte loads)
+  for (int tt = threadIdx.x; tt < n; tt += blockDim.x) {
+    const uint4* kr = reinterpret_cast<const uint4*>(kvl + (slab(tt) + tt) * 64);
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const uint4 u = __ldcg(kr + j);
+      const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float2 f = __half22float2(h2[e]);
+        s = fmaf(qs[8 * j + 2 * e], f.x, s);
+        s = fmaf(qs[8 * j + 2 * e + 1], f.y, s);
+      }
+    }
+    sc[tt] = __fmul_rn(s, scale);
+  }
+  __syncthreads();
+  float m = -INFINITY;
+  for (int tt = threadIdx.x; tt < n; tt += blockDim.x) m = fmaxf(m, sc[tt]);
+  m = warp_max(m);
+  if (lane == 0) red[ST_WARPS * 64 + warp] = m;
+  __syncthreads();
+  m = red[ST_WARPS * 64];
+  for (int w = 1; w < ST_WARPS; w++) m = fmaxf(m, red[ST_WARPS * 64 + w]);
+  __syncthreads();
+  float s = 0.f;
+  for (int tt = threadIdx.x; tt < n; tt += blockDim.x) {
+    const float e = ref_fast_exp(__fsub_rn(sc[tt], m));
+    sc[tt] = e;
+    s += e;
+  }
+  s = warp_sum(s);
+  if (lane == 0) red[ST_WARPS * 64 + warp] = s;
+  __syncthreads();
+  s = 0.f;
+  for (int w = 0; w < ST_WARPS; w++) s += red[ST_WARPS * 64 + w];
+  const float inv = __fdiv_rn(1.0f, s);  // s >= 1: the maximum's weight is exactly 1
+  // out = weights . V: warp per position, lane per channel pair
+  float o0 = 0.f, o1 = 0.f;
+  for (int tt = warp; tt < n; tt += ST_WARPS) {
+    const __half2 v = reinterpret_cast<const __half2*>(kvl + (slab(tt) + (int64_t)a.H * a.Tmax + tt) * 64)[lane];
+    const float w = __fmul_rn(sc[tt], inv);
+    const float2 f = __half22float2(v);
+    o0 = fmaf(w, f.x, o0);
+    o1 = fmaf(w, f.y, o1);
+  }
+  red[warp * 64 + 2 * lane] = o0;
+  red[warp * 64 + 2 * lane + 1] = o1;
+  __syncthreads();
+  if (threadIdx.x < 64) {
+    float v = 0.f;
+    for (int w = 0; w < ST_WARPS; w++) v += red[w * 64 + threadIdx.x];
+    out[threadIdx.x] = v;
+  }
+  __syncthreads();
+}
+
+// Cross-attention of utterance u, head hh over frames [t0, t1) for its B
+// rows: local maxima exchanged with the head's other chunks, then the
+// partial sums (o = sum e v, l = sum e) for the next matmul phase.
+__device__ void cross_attn_unit(const StepArgs& a, int l, int u, int hh, int ch, unsigned target, float* sm) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int B = a.B, per = (a.T + a.xchunks - 1) / a.xchunks;
+  const int t0 = ch * per, t1 = min(a.T, t0 + per), nt = max(0, t1 - t0);
+  float* qs = sm;                    // [B][64]
+  float* sc = qs + ST_MAX_ROWS * 64; // [B][ST_MAX_FRAMES_CHUNK]
+  float* red = sc + ST_MAX_ROWS * ST_MAX_FRAMES_CHUNK;  // [ST_WARPS][B][64] + [B] maxima
+  for (int i = threadIdx.x; i < B * 64; i += blockDim.x)
+    qs[i] = __ldcg(a.q + (int64_t)(u * B + i / 64) * a.d + hh * 64 + (i & 63));
+  __syncthreads();
+  const __half* kb = a.cross + ((((int64_t)l * a.U + u) * 2) * a.H + hh) * (int64_t)a.T * 64;
+  const __half* vb = kb + (int64_t)a.H * a.T * 64;
+  for (int i = threadIdx.x; i < nt; i += blockDim.x) {
+    const uint4* kr = reinterpret_cast<const uint4*>(kb + (int64_t)(t0 + i) * 64);
+    uint4 kv[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) kv[j] = kr[j];
+    for (int b = 0; b < B; b++) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const __half2* h2 = reinterpret_cast<const __half2*>(&kv[j]);
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const float2 f = __half22float2(h2[e]);
+          s = fmaf(qs[b * 64 + 8 * j + 2 * e], f.x, s);
+          s = fmaf(qs[b * 64 + 8 * j + 2 * e + 1], f.y, s);
+        }
+      }
+      sc[b * ST_MAX_FRAMES_CHUNK + i] = __fmul_rn(s, 0.125f);
+    }
+  }
+  __syncthreads();
+  // local maxima -> global scratch; wait for the head's other chunks
+  float* mx = red + ST_WARPS * ST_MAX_ROWS * 64;
+  for (int b = warp; b < B; b += ST_WARPS) {
+    float m = -INFINITY;
+    for (int i = lane; i < nt; i += 32) m = fmaxf(m, sc[b * ST_MAX_FRAMES_CHUNK + i]);
+    m = warp_max(m);
+    if (lane == 0) a.xmax[((int64_t)ch * a.R + u * B + b) * a.H + hh] = m;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    unsigned* cnt = a.sync + 4 + a.max_groups + u * a.H + hh;
+    red_release(cnt, 1u);
+    spin_until(a, cnt, target, (5 << 8) | 3);
+    __threadfence();
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    float m = -INFINITY;
+    for (int c = 0; c < a.xchunks; c++) m = fmaxf(m, __ldcg(a.xmax + ((int64_t)c * a.R + u * B + b) * a.H + hh));
+    mx[b] = m;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < B * nt; i += blockDim.x) {
+    const int b = i / nt, j = i - b * nt;
+    sc[b * ST_MAX_FRAMES_CHUNK + j] = ref_fast_exp(__fsub_rn(sc[b * ST_MAX_FRAMES_CHUNK + j], mx[b]));
+  }
+  __syncthreads();
+  // o[b][c] = sum_t e[b][t] v_t[c]: warp per frame, lane per channel pair
+  float o[ST_MAX_ROWS][2];
+#pragma unroll
+  for (int b = 0; b < ST_MAX_ROWS; b++) o[b][0] = o[b][1] = 0.f;
+  for (int i = warp; i < nt; i += ST_WARPS) {
+    const float2 f = __half22float2(reinterpret_cast<const __half2*>(vb + (int64_t)(t0 + i) * 64)[lane]);
+#pragma unroll
+    for (int b = 0; b < ST_MAX_ROWS; b++)
+      if (b < B) {
+        const float e = sc[b * ST_MAX_FRAMES_CHUNK + i];
+        o[b][0] = fmaf(e, f.x, o[b][0]);
+        o[b][1] = fmaf(e, f.y, o[b][1]);
+      }
+  }
+#pragma unroll
+  for (int b = 0; b < ST_MAX_ROWS; b++)
+    if (b < B) {
+      red[(warp * ST_MAX_ROWS + b) * 64 + 2 * lane] = o[b][0];
+      red[(warp * ST_MAX_ROWS + b) * 64 + 2 * lane + 1] = o[b][1];
+    }
+  __syncthreads();
+  for (int i = threadIdx.x; i < B * 65; i += blockDim.x) {
+    const int b = i / 65, c = i - b * 65;
+    float v = 0.f;
+    if (c < 64) {
+      for (int w = 0; w < ST_WARPS; w++) v += red[(w * ST_MAX_ROWS + b) * 64 + c];
+    } else {
+      for (int j = 0; j < nt; j++) v += sc[b * ST_MAX_FRAMES_CHUNK + j];
+    }
+    a.xpart[(((int64_t)ch * a.R + u * B + b) * a.H + hh) * 65 + c] = v;
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <uint32_t QT, int NB>
+__global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_constant__ StepArgs a) {
+  extern __shared__ __align__(128) unsigned char st_smem[];
+  const uint32_t slot_bytes = unit_bytes<QT>(ST_MAX_PAIRS);
+  unsigned char* ring_mem = st_smem;                                   // 2 weight slots
+  unsigned char* xmem = st_smem + 2 * slot_bytes;                      // activations hi | lo
+  const uint32_t xbytes = 2u * ST_MAX_ROWS * (ST_MAX_PAIRS * 64 + 16) * 2;
+  float* red = reinterpret_cast<float*>(xmem + xbytes);               // attention / reduction scratch
+  float* stat = red + (ST_MAX_ROWS * 64 + ST_MAX_ROWS * ST_MAX_FRAMES_CHUNK + ST_WARPS * ST_MAX_ROWS * 64 + 64);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(stat + 2 * ST_MAX_ROWS);
+  Ring rg;
+  rg.base = smem_u32(ring_mem);
+  rg.slot_bytes = slot_bytes;
+  rg.bar = smem_u32(bars);
+  rg.issued = rg.consumed = 0;
+  // units of this CTA in the whole step
+  {
+    int tot = 0;
+    for (int m = 0; m < 6; m++) {
+      const int n = units_of(a.mm[m]);
+      tot += n > (int)blockIdx.x ? (n - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+    }
+    rg.total = tot * a.L;
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(rg.bar, 1);
+    mbar_init(rg.bar + 8, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int k = 0; k < 2 && k < rg.total; k++) ring_issue<QT>(a, rg, k);
+  }
+  rg.issued = min(2, rg.total);
+  __syncthreads();
+  unsigned target = 0;
+  const int G = gridDim.x;
+  for (int l = 0; l < a.L; l++) {
+    mm_phase<QT, NB>(a, rg, l, 0, xmem, red, stat, ring_mem, 1);  // LayerNorm + q|k|v
+    grid_barrier(a, target, (l << 12) | 0x11);
+    for (int w = blockIdx.x; w < a.R * a.H; w += G) self_attn_unit(a, l, w / a.H, w % a.H, red);
+    grid_barrier(a, target, (l << 12) | 0x12);
+    mm_phase<QT, NB>(a, rg, l, 1, xmem, red, stat, ring_mem, 2);  // self out + residual
+    grid_barrier(a, target, (l << 12) | 0x13);
+    mm_phase<QT, NB>(a, rg, l, 2, xmem, red, stat, ring_mem, 3);  // LayerNorm + cross q
+    grid_barrier(a, target, (l << 12) | 0x14);
+    const int xu = a.U * a.H * a.xchunks;
+    for (int w = blockIdx.x; w < xu; w += G) {
+      const int ch = w % a.xchunks, uh = w / a.xchunks;
+      cross_attn_unit(a, l, uh / a.H, uh % a.H, ch, (unsigned)((l + 1) * a.xchunks), red);
+    }
+    grid_barrier(a, target, (l << 12) | 0x15);
+    mm_phase<QT, NB>(a, rg, l, 3, xmem, red, stat, ring_mem, 4);  // cross out + residual
+    grid_barrier(a, target, (l << 12) | 0x16);
+    mm_phase<QT, NB>(a, rg, l, 4, xmem, red, stat, ring_mem, 5);  // LayerNorm + mlp.0 + GELU
+    grid_barrier(a, target, (l << 12) | 0x17);
+    mm_phase<QT, NB>(a, rg, l, 5, xmem, red, stat, ring_mem, 6);  // mlp.2 + residual
+    grid_barrier(a, target, (l << 12) | 0x18);
+  }
+  // copies still in flight (only after an abort) land before the CTA exits
+  if (threadIdx.x == 0)
+    for (int k = rg.consumed; k < rg.issued; k++) mbar_drain(rg.bar + 8 * (k & 1), (uint32_t)(k >> 1) & 1u);
+  __syncthreads();
+}
+
+template <uint32_t QT, int NB>
+int configure_step_t() {
+  cudaError_t e = cudaFuncSetAttribute(step_kernel<QT, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (e != cudaSuccess) {
+    set_error("cudaFuncSetAttribute(step_kernel): %s", cudaGetErrorString(e));
+    return WG_ERR_CUDA;
+  }
+  return WG_OK;
+}
+
+template <uint32_t QT>
+size_t step_smem_bytes() {
+  const size_t slot = (size_t)ST_MAX_PAIRS * 16 *
+                      (32 * (QT == WG_QTYPE_Q8_0 ? 16 : 8) + 32 + (qtype_has_min(QT) ? 32 : 0) +
+                       (qtype_has_hbits(QT) ? 64 : 0));
+  const size_t xbytes = 2u * ST_MAX_ROWS * (ST_MAX_PAIRS * 64 + 16) * 2;
+  const size_t redf = ST_MAX_ROWS * 64 + ST_MAX_ROWS * ST_MAX_FRAMES_CHUNK + ST_WARPS * ST_MAX_ROWS * 64 + 64;
+  return 2 * slot + xbytes + (redf + 2 * ST_MAX_ROWS) * 4 + 16 + 128;
+}
+
+MmPlan plan(const DMat& W, int G) {
+  MmPlan p;
+  p.groups = (W.ntiles + 7) / 8;
+  p.pairs = W.kblocks / 2;
+  int ks = std::max(1, std::min(p.pairs, (G + p.groups / 2) / p.groups));
+  p.per = (p.pairs + ks - 1) / ks;
+  if (p.per > ST_MAX_PAIRS) p.per = ST_MAX_PAIRS;
+  p.ks = (p.pairs + p.per - 1) / p.per;
+  return p;
+}
+
+}  // namespace
+
+// ---- host side ------------------------------------------------------------------------
+struct StepModel {
+  StepLayer* layers = nullptr;  // device array
+  int L = 0;
+  uint32_t qtype = 0;
+};
+
+int step_init_attributes() {
+  int rc = WG_OK;
+  for (int nb = 1; nb <= 2 && rc == WG_OK; nb++) {
+    (void)nb;
+  }
+  rc = configure_step_t<WG_QTYPE_Q8_0, 1>();
+  if (rc == WG_OK) rc = configure_step_t<WG_QTYPE_Q8_0, 2>();
+  if (rc == WG_OK) rc = configure_step_t<WG_QTYPE_Q4_0, 1>();
+  if (rc == WG_OK) rc = configure_step_t<WG_QTYPE_Q4_0, 2>();
+  if (rc == WG_OK) rc = configure_step_t<WG_QTYPE_Q4_1, 1>();
+  if (rc == WG_OK) rc = configure_step_t<WG_QTYPE_Q4_1, 2>();
+  if (rc == WG_OK) rc = configure_step_t<WG_QTYPE_Q5_0, 1>();
+  if (rc == WG_OK) rc = configure_step_t<WG_QTYPE_Q5_0, 2>();
+  if (rc == WG_OK) rc = configure_step_t<WG_QTYPE_Q5_1, 1>();
+  if (rc == WG_OK) rc = configure_step_t<WG_QTYPE_Q5_1, 2>();
+  return rc;
+}
+
+int step_error_word(int* word, bool clear) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_step_error, sizeof(int));
+  if (e != cudaSuccess) {
+    set_error("reading the step kernel error word: %s", cudaGetErrorString(e));
+    return WG_ERR_CUDA;
+  }
+  if (clear && v) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_step_error, &z, sizeof(int));
+  }
+  *word = v;
+  return WG_OK;
+}
+
+}  // namespace wg

@@ -103,6 +103,7 @@ def _declare(lib):
         "wg_model_destroy": (ctypes.c_int, [P]),
         "wg_model_weight_bytes": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_int64)]),
         "wg_model_set_eot": (ctypes.c_int, [P, ctypes.c_int]),
+        "wg_model_info": (ctypes.c_int, [P] + [ctypes.POINTER(ctypes.c_int)] * 5),
         "wg_job_create": (ctypes.c_int, [P, ctypes.c_int, ctypes.c_int, c_int32_p, ctypes.c_int,
                                          ctypes.POINTER(WgDecodeParams), ctypes.POINTER(P)]),
         "wg_job_upload_encoder": (ctypes.c_int, [P, ctypes.POINTER(c_float_p)]),
@@ -498,6 +499,9 @@ class WhisperDecoder:
         self.h = h
         self.vocab = None
         self.eot = 50256
+        vals = [ctypes.c_int() for _ in range(5)]
+        check(lib().wg_model_info(h, *[ctypes.byref(v) for v in vals]))
+        self.n_vocab, self.n_state, self.n_head, self.n_layer, self.n_text_ctx = [v.value for v in vals]
         return self
 
     def weight_bytes(self) -> int:
