@@ -340,16 +340,21 @@ def main():
     peak, peak_kind = peaks()
     classes = {}
     steps_done, _, _ = job.stats()
-    per_step_launches = {"gemv": 6 * cfg["L"], "self_attn": cfg["L"], "cross_attn": cfg["L"], "logits": 1}
-    for k in ("gemv", "self_attn", "cross_attn", "logits"):
+    # the kernel classes a token step runs: at <= 16 rows all layers are one
+    # persistent kernel ("step"), else separate matmul / attention kernels
+    step_kernel = job.uses_step_kernel()
+    main = ("step", "logits") if step_kernel else ("gemv", "self_attn", "cross_attn", "logits")
+    per_step_launches = {"gemv": 6 * cfg["L"], "self_attn": cfg["L"], "cross_attn": cfg["L"], "logits": 1, "step": 1}
+    for k in main:
         t, b = job.time_kernel(k, iters=3)
         classes[k] = {"ms_per_launch": t, "bytes_per_launch": b, "gbs": b / (t * 1e6) if t > 0 else None,
                       "ms_per_step": t * per_step_launches[k]}
-    for k in ("qkv", "self_out", "cross_q", "cross_out", "mlp0", "mlp2", "precompute"):
+    for k in ("precompute",) if step_kernel else ("qkv", "self_out", "cross_q", "cross_out", "mlp0", "mlp2",
+                                                  "precompute"):
         t, b = job.time_kernel(k, iters=3)
         classes[k] = {"ms_per_launch": t, "bytes_per_launch": b, "gbs": b / (t * 1e6) if t > 0 else None,
                       "ms_per_step": t * (cfg["L"] if k != "precompute" else 1.0 / max(steps_done, 1))}
-    dom = max(("gemv", "self_attn", "cross_attn", "logits"), key=lambda k: classes[k]["ms_per_step"])
+    dom = max(main, key=lambda k: classes[k]["ms_per_step"])
     dk = classes[dom]
     roofline = {"bound": "hbm", "kernel": dom, "achieved": dk["gbs"], "peak": peak, "unit": "GB/s",
                 "frac": dk["gbs"] / peak if dk["gbs"] else None, "traffic": TRAFFIC.get(dom),

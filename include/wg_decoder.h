@@ -221,6 +221,8 @@ int wg_job_timer(wg_job* j, int which, double* ms);
 int wg_job_destroy(wg_job* j);
 /* Token steps executed so far (max over utterances) and rows per step. */
 int wg_job_stats(const wg_job* j, int* steps_done, int* rows, int* max_tokens);
+/* 1 when the job's layers run as the persistent step kernel (<= 16 rows). */
+int wg_job_uses_step_kernel(const wg_job* j, int* on);
 
 /* One call = the whole Decode for U utterances: create, upload, start,
  * step to completion, result, destroy. */
@@ -326,6 +328,7 @@ enum {
   WG_KCLASS_CROSS_ATTN = 2,
   WG_KCLASS_LOGITS = 3,
   WG_KCLASS_PRECOMPUTE = 4,  /* cross K/V projection of all layers (once per decode) */
+  WG_KCLASS_STEP = 5,        /* the persistent kernel of all layers (jobs of <= 16 rows) */
   WG_KCLASS_MATMUL0 = 10     /* + k: only matmul k of {qkv, self out, cross q, cross out, mlp0, mlp2} */
 };
 /* Re-launches one kernel class over all layers of one step on the job's own

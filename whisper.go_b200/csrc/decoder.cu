@@ -66,6 +66,7 @@ struct DevModel {
   float* vec = nullptr;  // all fp32 vectors (LN, biases, positional embedding)
   const float *pos_emb = nullptr, *ln_w = nullptr, *ln_b = nullptr, *cross_vb = nullptr;
   int64_t weight_bytes = 0;
+  StepLayer* step_layers = nullptr;  // device copy of every layer's weights and vectors (step kernel)
 };
 
 }  // namespace
@@ -98,6 +99,11 @@ struct DevJob {
   int* ints = nullptr;
   float* floats = nullptr;
   float* split_ws = nullptr;  // tcgen05 split-K partial tiles (TC_SPLIT_WS_FLOATS)
+  // persistent step kernel (R <= 16): fp32 attention / MLP activations and scratch
+  bool use_step = false;
+  float *st_att = nullptr, *st_h = nullptr, *st_part = nullptr, *st_xpart = nullptr, *st_xmax = nullptr;
+  unsigned* st_sync = nullptr;
+  int* st_err = nullptr;
   SampleState ss{};
   int* host_done = nullptr;  // pinned
   cudaGraphExec_t graph = nullptr;
@@ -138,6 +144,13 @@ int64_t env_i64(const char* name, int64_t dflt) {
   return strtoll(v, nullptr, 10);
 }
 
+// WG_STEP_KERNEL=0 keeps every small-batch step on the separate kernels
+// (read at every forward pass, so a test can compare both in one process).
+bool env_step_enabled() {
+  const char* v = getenv("WG_STEP_KERNEL");
+  return !(v && v[0] == '0');
+}
+
 // Waits for a stream with the host watchdog deadline (WG_TIMEOUT_MS).
 // Error words of the kernels with bounded waits (current device): a wait
 // that expired means a copy or a peer never arrived; the step's results are
@@ -157,6 +170,11 @@ static int check_wait_flags() {
   WG_CHECK(gemv_error_word(&w, true));
   if (w) {
     set_error("a GEMV kernel's bounded wait expired (code 0x%x)", w);
+    return WG_ERR_DEVICE_FLAG;
+  }
+  WG_CHECK(step_error_word(&w, true));
+  if (w) {
+    set_error("the step kernel's bounded wait expired (code 0x%x)", w);
     return WG_ERR_DEVICE_FLAG;
   }
   return WG_OK;
@@ -192,6 +210,7 @@ void free_devmodel(DevModel* d) {
     free_dmat(l.qkv); free_dmat(l.so); free_dmat(l.cq); free_dmat(l.co); free_dmat(l.m0); free_dmat(l.m2);
   }
   cudaFree(d->vec);
+  cudaFree(d->step_layers);
   if (d->st) cudaStreamDestroy(d->st);
   delete d;
 }
@@ -207,6 +226,7 @@ int build_devmodel(const wg_model_desc* md, int dev, DevModel** out) {
   if ((rc = init_attn_attributes()) != WG_OK) return fail(rc);
   if ((rc = init_tc_attributes()) != WG_OK) return fail(rc);
   if ((rc = init_gemv_bulk_attributes()) != WG_OK) return fail(rc);
+  if ((rc = init_step_attributes()) != WG_OK) return fail(rc);
   const int d = md->n_state, L = md->n_layer, ctx = md->n_text_ctx;
   // fp32 vectors: 6 LN + 7 biases (d or 4d) per layer, final LN, pos emb, cross V bias
   std::vector<float> host;
@@ -261,6 +281,21 @@ int build_devmodel(const wg_model_desc* md, int dev, DevModel** out) {
     ckv.push_back(&s.cross_v);
   }
   if ((rc = upload_matrix(ckv.data(), (int)ckv.size(), &dm->cross_kv, dm->st)) != WG_OK) return fail(rc);
+  {  // the layers as the step kernel reads them
+    std::vector<StepLayer> sl(L);
+    for (int l = 0; l < L; l++) {
+      const DevLayer& o = dm->layers[l];
+      StepLayer& t = sl[l];
+      t.w[0] = o.qkv; t.w[1] = o.so; t.w[2] = o.cq; t.w[3] = o.co; t.w[4] = o.m0; t.w[5] = o.m2;
+      t.sln_w = o.sln_w; t.sln_b = o.sln_b; t.cln_w = o.cln_w; t.cln_b = o.cln_b; t.mln_w = o.mln_w; t.mln_b = o.mln_b;
+      t.q_b = o.q_b; t.v_b = o.v_b; t.so_b = o.so_b; t.cq_b = o.cq_b; t.co_b = o.co_b; t.m0_b = o.m0_b; t.m2_b = o.m2_b;
+    }
+    if (cudaMalloc(&dm->step_layers, sl.size() * sizeof(StepLayer)) != cudaSuccess ||
+        cudaMemcpy(dm->step_layers, sl.data(), sl.size() * sizeof(StepLayer), cudaMemcpyHostToDevice) != cudaSuccess) {
+      set_error("model upload: step layer table failed");
+      return fail(WG_ERR_OOM);
+    }
+  }
   int64_t wb = dmat_device_bytes(dm->tok) + dmat_device_bytes(dm->cross_kv);
   for (auto& l : dm->layers)
     wb += dmat_device_bytes(l.qkv) + dmat_device_bytes(l.so) + dmat_device_bytes(l.cq) + dmat_device_bytes(l.co) +
@@ -270,12 +305,44 @@ int build_devmodel(const wg_model_desc* md, int dev, DevModel** out) {
   return WG_OK;
 }
 
+// The persistent step kernel over all layers of a job's rows (step.cu).
+int launch_step_job(wg_model* m, DevJob& j, int mode) {
+  DevModel& dm = *j.dm;
+  const DevLayer& l0 = dm.layers[0];
+  const DMat* w0[6] = {&l0.qkv, &l0.so, &l0.cq, &l0.co, &l0.m0, &l0.m2};
+  StepArgs a{};
+  a.layers = dm.step_layers;
+  a.L = m->L; a.R = j.R; a.U = j.U; a.B = j.B; a.d = m->d; a.H = m->H; a.T = j.T; a.Tmax = j.Tmax;
+  a.pos = j.ss.pos;
+  const bool ref = mode == WG_MODE_REF_COMPAT;
+  a.tbl = (!ref && j.B > 1) ? j.ss.tbl : nullptr;
+  a.ref_compat = ref;
+  a.zero_unless_pos0 = ref && j.B > 1;
+  a.x = j.x; a.q = j.q; a.att = j.st_att; a.h = j.st_h;
+  a.selfkv = j.selfkv; a.cross = j.cross;
+  a.part = j.st_part; a.xpart = j.st_xpart; a.xmax = j.st_xmax; a.sync = j.st_sync; a.err = j.st_err;
+  return launch_step(a, w0, j.st);
+}
+
 // ---- one forward pass over all rows of a device job (decoder.go:745-833) ----
 int forward_step(wg_model* m, DevJob& j, const int* tokens, bool want_logits, int mode) {
   DevModel& dm = *j.dm;
   cudaStream_t st = j.st;
   const int d = m->d, H = m->H, hd = m->hd, R = j.R;
   WG_CHECK(launch_embed(dm.tok, dm.pos_emb, tokens, j.ss.pos, 0, R, d, j.x, st));
+  if (j.use_step && env_step_enabled()) {
+    // every layer in one persistent kernel (small batches)
+    WG_CHECK(launch_step_job(m, j, mode));
+    if (!want_logits) return WG_OK;
+    Epi e = job_epi(j);
+    if (matmul_fuses_input_ln(dm.tok, R)) {
+      e.ln_x = j.x; e.ln_w = dm.ln_w; e.ln_b = dm.ln_b; e.ln_d = d;
+    } else {
+      WG_CHECK(launch_layernorm(j.x, dm.ln_w, dm.ln_b, R, d, j.xln16, nullptr, st));
+    }
+    e.mode = EPI_F32; e.out = j.logits; e.ldo = m->V; e.N = m->V;
+    return launch_matmul(dm.tok, j.xln16, j.ldd, R, e, st);
+  }
   const int64_t layer_kv = (int64_t)R * 2 * H * j.Tmax * hd;
   const int64_t layer_cross = (int64_t)j.U * 2 * H * j.T * hd;
   const bool ref = mode == WG_MODE_REF_COMPAT;
@@ -348,6 +415,8 @@ void free_devjob(DevJob* j) {
   cudaFree(j->x); cudaFree(j->q); cudaFree(j->logits); cudaFree(j->xln16); cudaFree(j->attn16); cudaFree(j->h16);
   cudaFree(j->ptok); cudaFree(j->prompt_dev); cudaFree(j->forced_dev); cudaFree(j->ints); cudaFree(j->floats);
   cudaFree(j->split_ws);
+  cudaFree(j->st_att); cudaFree(j->st_h); cudaFree(j->st_part); cudaFree(j->st_xpart); cudaFree(j->st_xmax);
+  cudaFree(j->st_sync);
   if (j->host_done) cudaFreeHost(j->host_done);
   for (auto& e : j->ev)
     if (e) cudaEventDestroy(e);
@@ -409,6 +478,20 @@ int build_devjob(wg_job* J, DevModel* dm, const std::vector<int>& utt, DevJob** 
   if ((rc = dalloc(&j->ints, n_ints)) || (rc = dalloc(&j->floats, n_floats)) ||
       (rc = dalloc(&j->split_ws, (size_t)TC_SPLIT_WS_FLOATS)))
     return fail(rc);
+  {
+    const DevLayer& l0 = dm->layers[0];
+    const DMat* w0[6] = {&l0.qkv, &l0.so, &l0.cq, &l0.co, &l0.m0, &l0.m2};
+    if (step_supported(w0, R, hd, d, T, j->Tmax)) {
+      int64_t np = 0, nx = 0, nm = 0, ns = 0;
+      step_scratch_sizes(w0, R, U, H, T, &np, &nx, &nm, &ns);
+      if ((rc = dalloc(&j->st_att, (size_t)R * d)) || (rc = dalloc(&j->st_h, (size_t)R * 4 * d)) ||
+          (rc = dalloc(&j->st_part, (size_t)np)) || (rc = dalloc(&j->st_xpart, (size_t)nx)) ||
+          (rc = dalloc(&j->st_xmax, (size_t)nm)) || (rc = dalloc(&j->st_sync, (size_t)ns)) ||
+          (rc = step_error_ptr(&j->st_err)))
+        return fail(rc);
+      j->use_step = true;
+    }
+  }
   int* ip = j->ints;
   auto take = [&](size_t n) {
     int* p = ip;
@@ -529,6 +612,13 @@ int ensure_graph(wg_job* J, DevJob& j) {
   g_launches.store(before);
   if (rc != WG_OK || e != cudaSuccess) {
     if (g) cudaGraphDestroy(g);
+    if (j.use_step) {
+      // a runtime that cannot capture the cooperative step kernel: replay the
+      // step eagerly (a handful of launches per token step)
+      cudaGetLastError();
+      j.graph = nullptr;
+      return WG_OK;
+    }
     if (rc == WG_OK) set_error("graph capture failed: %s", cudaGetErrorString(e));
     return rc == WG_OK ? WG_ERR_CUDA : rc;
   }
@@ -538,6 +628,10 @@ int ensure_graph(wg_job* J, DevJob& j) {
   cudaGraphDestroy(g);
   if (e != cudaSuccess) {
     j.graph = nullptr;
+    if (j.use_step) {  // as above: eager replay
+      cudaGetLastError();
+      return WG_OK;
+    }
     set_error("cudaGraphInstantiate: %s", cudaGetErrorString(e));
     return WG_ERR_CUDA;
   }
@@ -958,6 +1052,12 @@ int wg_job_destroy(wg_job* J) {
   return WG_OK;
 }
 
+int wg_job_uses_step_kernel(const wg_job* J, int* on) {
+  if (!J || !on) return WG_ERR_INVALID;
+  *on = !J->dj.empty() && J->dj[0]->use_step && env_step_enabled();
+  return WG_OK;
+}
+
 int wg_job_stats(const wg_job* J, int* steps_done, int* rows, int* max_tokens) {
   if (!J) return WG_ERR_INVALID;
   if (steps_done) *steps_done = J->steps_done;
@@ -1218,6 +1318,21 @@ int wg_job_time_kernel(wg_job* J, int kclass, int iters, double* ms, double* byt
         WG_CHECK(launch_matmul(dm.cross_kv, j.enc16, j.ldd, j.U * j.T, e, j.st));
         if (count) {
           b += (double)dmat_device_bytes(dm.cross_kv) + (double)j.U * j.T * d * 2 + (double)j.U * j.T * 2 * L * d * 2;
+          launches++;
+        }
+      } else if (kclass == WG_KCLASS_STEP) {
+        if (l > 0) break;
+        if (!j.use_step) {
+          set_error("wg_job_time_kernel: this job does not use the step kernel");
+          return WG_ERR_INVALID;
+        }
+        WG_CHECK(launch_step_job(m, j, J->mode));
+        if (count) {
+          for (const DevLayer& ly : dm.layers)
+            b += (double)dmat_device_bytes(ly.qkv) + dmat_device_bytes(ly.so) + dmat_device_bytes(ly.cq) +
+                 dmat_device_bytes(ly.co) + dmat_device_bytes(ly.m0) + dmat_device_bytes(ly.m2);
+          const int n_att = ref ? 1 : pos_h + 1;
+          b += (double)R * L * n_att * H * hd * 2 * 2 + (double)j.U * L * 2 * j.T * d * 2;
           launches++;
         }
       } else if (kclass == WG_KCLASS_LOGITS) {

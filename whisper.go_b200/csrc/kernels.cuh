@@ -121,6 +121,54 @@ int launch_cross_attn(const CrossAttnArgs& a, cudaStream_t st);
 int attn_error_word(int* word, bool clear);
 int init_attn_attributes();
 
+// ---- the persistent token-step kernel (step.cu) --------------------------------------
+// Layer weights and vectors as the step kernel reads them (device array, one per layer).
+struct StepLayer {
+  DMat w[6];  // q|k|v, self out, cross q, cross out, mlp.0, mlp.2
+  const float *sln_w, *sln_b, *cln_w, *cln_b, *mln_w, *mln_b;
+  const float *q_b, *v_b, *so_b, *cq_b, *co_b, *m0_b, *m2_b;
+};
+// One matmul of the step: 128-row groups, 64-wide K pairs, K splits, pairs per split.
+struct MmPlan {
+  int groups, pairs, ks, per;
+};
+struct StepArgs {
+  const StepLayer* layers;
+  int L, R, U, B, d, H, T, Tmax;
+  MmPlan mm[6];
+  int xchunks;                 // frame chunks per cross-attention head
+  const int* pos;              // device scalar
+  const int* tbl;              // [R][Tmax] physical row of each position (beams, CORRECT) or nullptr
+  int ref_compat, zero_unless_pos0;
+  float* x;                    // [R][d] residual stream (embedding already added)
+  float* q;                    // [R][d] self-attention q, then cross-attention q
+  float* att;                  // [R][d] self-attention output
+  float* h;                    // [R][4d] GELU(mlp.0)
+  __half* selfkv;              // [L][R][2][H][Tmax][64]
+  const __half* cross;         // [L][U][2][H][T][64]
+  float* part;                 // matmul partial tiles [group * ks + split][R][128]
+  float* xpart;                // cross-attention partials [chunk][R][H][65] (o[64], l)
+  float* xmax;                 // [chunk][R][H] per-chunk maxima
+  unsigned* sync;              // [0] barrier, [1] unused, [2] abort, [4, 4 + max_groups) group counters,
+                               // then [U * H] head counters; zero before every launch
+  int max_groups;
+  int* err;                    // the step kernel's error word (step_error_word)
+};
+// Whether the step kernel can run this model at R rows (weights of one
+// quantised type, K % 64 == 0, head dim 64, R <= 16; WG_STEP_KERNEL=0: never).
+bool step_supported(const DMat* const w0[6], int R, int hd, int d, int T, int Tmax);
+// Scratch of a job using the step kernel: floats of part / xpart / xmax and
+// unsigned of sync.
+void step_scratch_sizes(const DMat* const w0[6], int R, int U, int H, int T, int64_t* part, int64_t* xpart,
+                        int64_t* xmax, int64_t* sync);
+// Plans (matmul splits, frame chunks) and the cooperative launch on st; the
+// caller fills every other field of a.
+int launch_step(StepArgs a, const DMat* const w0[6], cudaStream_t st);
+int init_step_attributes();
+int step_error_word(int* word, bool clear);
+// Device address of the step kernel's error word (current device).
+int step_error_ptr(int** p);
+
 // ---- sampling (sample.cu) ----------------------------------------------------------
 struct SampleState {
   int R, B, U;             // rows, beam width (1 = greedy), utterances

@@ -49,45 +49,11 @@ namespace {
 
 constexpr int ST_WARPS = 8;  // one per 16-row tile of a 128-row group
 constexpr int ST_THREADS = ST_WARPS * 32;
-constexpr int ST_MAX_PAIRS = 8;  // 64-wide K chunks of one matmul unit
+constexpr int ST_MAX_PAIRS = 6;  // 64-wide K chunks of one matmul unit
 constexpr int ST_MAX_ROWS = 16;
 constexpr int ST_MAX_CHUNKS = 8;  // frame chunks of one cross-attention head
 constexpr int ST_MAX_POS = 448;   // KV positions (n_text_ctx)
-constexpr int ST_MAX_FRAMES_CHUNK = 512;
-
-// Layer weights and vectors as the kernel reads them (device array).
-struct StepLayer {
-  DMat w[6];  // q|k|v, self out, cross q, cross out, mlp.0, mlp.2
-  const float *sln_w, *sln_b, *cln_w, *cln_b, *mln_w, *mln_b;
-  const float *q_b, *v_b, *so_b, *cq_b, *co_b, *m0_b, *m2_b;
-};
-
-// One matmul of the step: its K split and the units it has.
-struct MmPlan {
-  int groups, pairs, ks, per;  // 128-row groups, 64-wide K pairs, K splits, pairs per split
-};
-
-struct StepArgs {
-  const StepLayer* layers;
-  int L, R, U, B, d, H, T, Tmax;
-  MmPlan mm[6];
-  int xchunks;                 // frame chunks per cross-attention head
-  const int* pos;              // device scalar
-  const int* tbl;              // [R][Tmax] physical row of each position (beams, CORRECT) or nullptr
-  int ref_compat, zero_unless_pos0;
-  float* x;                    // [R][d] residual stream (embedding already added)
-  float* q;                    // [R][d] self-attention q, then cross-attention q
-  float* att;                  // [R][d] self-attention output
-  float* h;                    // [R][4d] GELU(mlp.0)
-  __half* selfkv;              // [L][R][2][H][Tmax][64]
-  const __half* cross;         // [L][U][2][H][T][64]
-  float* part;                 // matmul partial tiles [unit][R][128]
-  float* xpart;                // cross-attention partials [chunk][R][H][65] (o[64], l)
-  float* xmax;                 // [chunk][R][H] per-chunk maxima
-  unsigned* sync;              // [0] grid barrier, [1] exits, [2] abort, [4..4+G) group counters, then [U*H] head counters
-  int max_groups;
-  int* err;
-};
+constexpr int ST_MAX_FRAMES_CHUNK = 256;
 
 // ---------------------------------------------------------------------------
 // synchronisation (all waits bounded: 2 s of %globaltimer)
@@ -102,7 +68,6 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
 __device__ __forceinline__ void red_release(unsigned* p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ bool aborted(const StepArgs& a) { return ld_acquire(a.sync + 2) != 0; }
 __device__ void raise_abort(const StepArgs& a, int code) {
   atomicCAS(a.err, 0, code);
   atomicExch(a.sync + 2, 1u);
@@ -145,29 +110,20 @@ struct Ring {
   uint32_t bar;            // two mbarriers
   int issued, consumed;    // units issued / consumed so far
   int total;               // units of this CTA in the step
-};
-
-// Unit u of the CTA's sequence -> (layer, matrix, group, k split).
-struct UnitRef {
-  int l, m, g, kz;
+  int cl, cm, cu;          // issue cursor (thread 0): layer, matmul, unit of the next copy
 };
 
 __device__ __forceinline__ int units_of(const MmPlan& p) { return p.groups * p.ks; }
-// the k-th unit (k >= 0) this CTA processes in the step, or l = -1 past the end
-__device__ UnitRef unit_at(const StepArgs& a, int k) {
-  const int G = gridDim.x, b = blockIdx.x;
-  int left = k;
-  for (int l = 0; l < a.L; l++)
-    for (int m = 0; m < 6; m++) {
-      const int n = units_of(a.mm[m]);
-      const int mine = n > b ? (n - b + G - 1) / G : 0;  // units b, b+G, ...
-      if (left < mine) {
-        const int u = b + left * G;
-        return UnitRef{l, m, u / a.mm[m].ks, u % a.mm[m].ks};
-      }
-      left -= mine;
+
+// Moves the cursor to the next unit of this CTA at or after (cl, cm, cu).
+__device__ void cursor_fix(const StepArgs& a, Ring& rg) {
+  while (rg.cl < a.L && rg.cu >= units_of(a.mm[rg.cm])) {
+    if (++rg.cm == 6) {
+      rg.cm = 0;
+      rg.cl++;
     }
-  return UnitRef{-1, 0, 0, 0};
+    rg.cu = blockIdx.x;
+  }
 }
 
 template <uint32_t QT>
@@ -178,19 +134,21 @@ __device__ __forceinline__ uint32_t unit_bytes(int np) {
   return (uint32_t)np * 16 * (32 * pb + 32 + (has_m ? 32 : 0) + (has_h ? 64 : 0));
 }
 
-// Issues unit k's copies into slot k % 2 (thread 0; the slot is free).
+// Issues the copies of the cursor's unit (the CTA's unit number rg.issued)
+// into slot issued % 2, which is free, and advances the cursor (thread 0).
 template <uint32_t QT>
-__device__ void ring_issue(const StepArgs& a, Ring& rg, int k) {
-  const UnitRef ur = unit_at(a, k);
-  if (ur.l < 0) return;
+__device__ void ring_issue(const StepArgs& a, Ring& rg) {
+  if (rg.cl >= a.L) return;
   constexpr uint32_t pb = QT == WG_QTYPE_Q8_0 ? 16 : 8;
   constexpr bool has_m = QT == WG_QTYPE_Q4_1 || QT == WG_QTYPE_Q5_1;
   constexpr bool has_h = QT == WG_QTYPE_Q5_0 || QT == WG_QTYPE_Q5_1;
-  const MmPlan& pl = a.mm[ur.m];
-  const DMat& W = a.layers[ur.l].w[ur.m];
-  const int p0 = ur.kz * pl.per, np = min(pl.per, pl.pairs - p0);
+  const MmPlan& pl = a.mm[rg.cm];
+  const DMat& W = a.layers[rg.cl].w[rg.cm];
+  const int g = rg.cu / pl.ks, kz = rg.cu % pl.ks;
+  const int p0 = kz * pl.per, np = min(pl.per, pl.pairs - p0);
   const uint32_t slots = (uint32_t)np * 16;
-  const int64_t S0 = ((int64_t)ur.g * pl.pairs + p0) * 16;
+  const int64_t S0 = ((int64_t)g * pl.pairs + p0) * 16;
+  const int k = rg.issued;
   const uint32_t dst = rg.base + (uint32_t)(k & 1) * rg.slot_bytes, bar = rg.bar + 8 * (k & 1);
   const uint32_t qb = slots * 32 * pb;
   mbar_arrive_tx(bar, unit_bytes<QT>(np));
@@ -202,6 +160,8 @@ __device__ void ring_issue(const StepArgs& a, Ring& rg, int k) {
     o += slots * 32;
   }
   if (has_h) bulk_g2s(dst + o, W.hb + S0 * 32, slots * 64, bar);
+  rg.cu += gridDim.x;
+  cursor_fix(a, rg);
 }
 
 // ---------------------------------------------------------------------------
@@ -267,9 +227,13 @@ __device__ void stage_x(const StepArgs& a, int src, const float* lnw, const floa
 // ---------------------------------------------------------------------------
 // one matmul unit: partial tile, then (last arriver of its group) the epilogue
 // ---------------------------------------------------------------------------
+struct UnitRef {
+  int l, m, g, kz;
+};
+
 template <uint32_t QT, int NB>
 __device__ void mm_unit(const StepArgs& a, const UnitRef& ur, const unsigned char* wsm, unsigned char* smem_x,
-                        float* red, const float* stat, unsigned& ok_flag) {
+                        const float* stat) {
   constexpr int RC = NB * 8;
   constexpr int pb = QT == WG_QTYPE_Q8_0 ? 16 : 8;
   constexpr bool has_m = QT == WG_QTYPE_Q4_1 || QT == WG_QTYPE_Q5_1;
@@ -376,13 +340,12 @@ __device__ void mm_unit(const StepArgs& a, const UnitRef& ur, const unsigned cha
       default: a.x[(int64_t)r * a.d + n] = __fadd_rn(__ldcg(a.x + (int64_t)r * a.d + n), __fadd_rn(v, ly.m2_b[n])); break;
     }
   }
-  (void)ok_flag;
 }
 
 // All of this CTA's units of matmul m of layer l.
 template <uint32_t QT, int NB>
-__device__ void mm_phase(const StepArgs& a, Ring& rg, int l, int m, unsigned char* smem_x, float* red, float* stat,
-                         unsigned char* smem, int phase_code) {
+__device__ void mm_phase(const StepArgs& a, Ring& rg, int l, int m, unsigned char* smem_x, float* stat,
+                         unsigned char* ring_mem, int phase_code) {
   const MmPlan& pl = a.mm[m];
   const int n = units_of(pl);
   if ((int)blockIdx.x >= n) return;
@@ -390,11 +353,10 @@ __device__ void mm_phase(const StepArgs& a, Ring& rg, int l, int m, unsigned cha
     ln_stats(a, stat);
     __syncthreads();
   }
-  unsigned okf = 1;
+  __shared__ int wok;
   for (int u = blockIdx.x; u < n; u += gridDim.x) {
     const int k = rg.consumed;
-    // the unit's weights: wait for the slot's copy
-    __shared__ int wok;
+    // the unit's weights: wait for the slot's copies
     if (threadIdx.x == 0) {
       wok = mbar_wait(rg.bar + 8 * (k & 1), (uint32_t)(k >> 1) & 1u, reinterpret_cast<volatile int*>(a.sync + 2),
                       (phase_code << 8) | 1, a.err);
@@ -403,11 +365,13 @@ __device__ void mm_phase(const StepArgs& a, Ring& rg, int l, int m, unsigned cha
     __syncthreads();
     if (!wok) return;
     const UnitRef ur{l, m, u / pl.ks, u % pl.ks};
-    mm_unit<QT, NB>(a, ur, smem + (uint32_t)(k & 1) * rg.slot_bytes, smem_x, red, stat, okf);
-    __syncthreads();  // every warp is done with the slot
+    mm_unit<QT, NB>(a, ur, ring_mem + (uint32_t)(k & 1) * rg.slot_bytes, smem_x, stat);
+    __syncthreads();  // every warp is done with the slot: refill it
     rg.consumed++;
-    if (threadIdx.x == 0 && rg.issued < rg.total) ring_issue<QT>(a, rg, rg.issued);
-    rg.issued = min(rg.issued + 1, rg.total);
+    if (rg.issued < rg.total) {
+      if (threadIdx.x == 0) ring_issue<QT>(a, rg);
+      rg.issued++;
+    }
   }
 }
 
@@ -476,7 +440,7 @@ __device__ void self_attn_unit(const StepArgs& a, int l, int r, int hh, float* s
   // out = weights . V: warp per position, lane per channel pair
   float o0 = 0.f, o1 = 0.f;
   for (int tt = warp; tt < n; tt += ST_WARPS) {
-    const __half2 v = reinterpret_cast<const __half2*>(kvl + (slab(tt) + (int64_t)a.H * a.Tmax + tt) * 64)[lane];
+    const __half2 v = __ldcg(reinterpret_cast<const __half2*>(kvl + (slab(tt) + (int64_t)a.H * a.Tmax + tt) * 64) + lane);
     const float w = __fmul_rn(sc[tt], inv);
     const float2 f = __half22float2(v);
     o0 = fmaf(w, f.x, o0);
@@ -609,8 +573,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   rg.slot_bytes = slot_bytes;
   rg.bar = smem_u32(bars);
   rg.issued = rg.consumed = 0;
-  // units of this CTA in the whole step
-  {
+  rg.cl = 0;
+  rg.cm = 0;
+  rg.cu = blockIdx.x;
+  cursor_fix(a, rg);
+  {  // units of this CTA in the whole step
     int tot = 0;
     for (int m = 0; m < 6; m++) {
       const int n = units_of(a.mm[m]);
@@ -622,32 +589,37 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
     mbar_init(rg.bar, 1);
     mbar_init(rg.bar + 8, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    for (int k = 0; k < 2 && k < rg.total; k++) ring_issue<QT>(a, rg, k);
   }
-  rg.issued = min(2, rg.total);
   __syncthreads();
+  for (int k = 0; k < 2 && rg.issued < rg.total; k++) {
+    if (threadIdx.x == 0) ring_issue<QT>(a, rg);
+    rg.issued++;
+  }
   unsigned target = 0;
   const int G = gridDim.x;
   for (int l = 0; l < a.L; l++) {
-    mm_phase<QT, NB>(a, rg, l, 0, xmem, red, stat, ring_mem, 1);  // LayerNorm + q|k|v
+    mm_phase<QT, NB>(a, rg, l, 0, xmem, stat, ring_mem, 1);  // LayerNorm + q|k|v
     grid_barrier(a, target, (l << 12) | 0x11);
     for (int w = blockIdx.x; w < a.R * a.H; w += G) self_attn_unit(a, l, w / a.H, w % a.H, red);
     grid_barrier(a, target, (l << 12) | 0x12);
-    mm_phase<QT, NB>(a, rg, l, 1, xmem, red, stat, ring_mem, 2);  // self out + residual
+    mm_phase<QT, NB>(a, rg, l, 1, xmem, stat, ring_mem, 2);  // self out + residual
     grid_barrier(a, target, (l << 12) | 0x13);
-    mm_phase<QT, NB>(a, rg, l, 2, xmem, red, stat, ring_mem, 3);  // LayerNorm + cross q
+    mm_phase<QT, NB>(a, rg, l, 2, xmem, stat, ring_mem, 3);  // LayerNorm + cross q
     grid_barrier(a, target, (l << 12) | 0x14);
-    const int xu = a.U * a.H * a.xchunks;
-    for (int w = blockIdx.x; w < xu; w += G) {
+    // rounds of whole heads: the chunks of a head exchange maxima and wait
+    // for one another, so they must all run in the same round (no CTA may
+    // wait on a chunk that another CTA only reaches in a later round)
+    const int xu = a.U * a.H * a.xchunks, per_round = (G / a.xchunks) * a.xchunks;
+    for (int w = blockIdx.x; (int)blockIdx.x < per_round && w < xu; w += per_round) {
       const int ch = w % a.xchunks, uh = w / a.xchunks;
       cross_attn_unit(a, l, uh / a.H, uh % a.H, ch, (unsigned)((l + 1) * a.xchunks), red);
     }
     grid_barrier(a, target, (l << 12) | 0x15);
-    mm_phase<QT, NB>(a, rg, l, 3, xmem, red, stat, ring_mem, 4);  // cross out + residual
+    mm_phase<QT, NB>(a, rg, l, 3, xmem, stat, ring_mem, 4);  // cross out + residual
     grid_barrier(a, target, (l << 12) | 0x16);
-    mm_phase<QT, NB>(a, rg, l, 4, xmem, red, stat, ring_mem, 5);  // LayerNorm + mlp.0 + GELU
+    mm_phase<QT, NB>(a, rg, l, 4, xmem, stat, ring_mem, 5);  // LayerNorm + mlp.0 + GELU
     grid_barrier(a, target, (l << 12) | 0x17);
-    mm_phase<QT, NB>(a, rg, l, 5, xmem, red, stat, ring_mem, 6);  // mlp.2 + residual
+    mm_phase<QT, NB>(a, rg, l, 5, xmem, stat, ring_mem, 6);  // mlp.2 + residual
     grid_barrier(a, target, (l << 12) | 0x18);
   }
   // copies still in flight (only after an abort) land before the CTA exits
@@ -656,9 +628,13 @@ __global__ void __launch_bounds__(ST_THREADS, 1) step_kernel(const __grid_consta
   __syncthreads();
 }
 
+template <uint32_t QT>
+size_t step_smem_bytes();
+
 template <uint32_t QT, int NB>
 int configure_step_t() {
-  cudaError_t e = cudaFuncSetAttribute(step_kernel<QT, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaError_t e =
+      cudaFuncSetAttribute(step_kernel<QT, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)step_smem_bytes<QT>());
   if (e != cudaSuccess) {
     set_error("cudaFuncSetAttribute(step_kernel): %s", cudaGetErrorString(e));
     return WG_ERR_CUDA;
@@ -676,7 +652,7 @@ size_t step_smem_bytes() {
   return 2 * slot + xbytes + (redf + 2 * ST_MAX_ROWS) * 4 + 16 + 128;
 }
 
-MmPlan plan(const DMat& W, int G) {
+MmPlan plan_of(const DMat& W, int G) {
   MmPlan p;
   p.groups = (W.ntiles + 7) / 8;
   p.pairs = W.kblocks / 2;
@@ -687,21 +663,96 @@ MmPlan plan(const DMat& W, int G) {
   return p;
 }
 
+int xchunks_of(int U, int H, int T, int G) {
+  int c = std::max(1, G / std::max(1, U * H));
+  c = std::max(c, (T + ST_MAX_FRAMES_CHUNK - 1) / ST_MAX_FRAMES_CHUNK);
+  return std::min(c, ST_MAX_CHUNKS);
+}
+
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <uint32_t QT>
+int launch_step_q(const StepArgs& a, cudaStream_t st) {
+  const size_t smem = step_smem_bytes<QT>();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sm_count(), 1, 1);
+  cfg.blockDim = dim3(ST_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeCooperative;  // every CTA resident at once: the grid barrier can complete
+  at[0].val.cooperative = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaError_t e = a.R <= 8 ? cudaLaunchKernelEx(&cfg, step_kernel<QT, 1>, a) : cudaLaunchKernelEx(&cfg, step_kernel<QT, 2>, a);
+  return launch_check(e, "step_kernel");
+}
+
 }  // namespace
 
-// ---- host side ------------------------------------------------------------------------
-struct StepModel {
-  StepLayer* layers = nullptr;  // device array
-  int L = 0;
-  uint32_t qtype = 0;
-};
-
-int step_init_attributes() {
-  int rc = WG_OK;
-  for (int nb = 1; nb <= 2 && rc == WG_OK; nb++) {
-    (void)nb;
+bool step_supported(const DMat* const w0[6], int R, int hd, int d, int T, int Tmax) {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("WG_STEP_KERNEL");
+    on = !(v && v[0] == '0');
   }
-  rc = configure_step_t<WG_QTYPE_Q8_0, 1>();
+  if (!on || R < 1 || R > ST_MAX_ROWS || hd != 64 || d % 64 || T < 1 || Tmax > ST_MAX_POS ||
+      (T + ST_MAX_FRAMES_CHUNK - 1) / ST_MAX_FRAMES_CHUNK > ST_MAX_CHUNKS || T > 4 * 1024)
+    return false;
+  for (int m = 0; m < 6; m++)
+    if (!qtype_is_quant(w0[m]->qtype) || w0[m]->qtype != w0[0]->qtype || w0[m]->cols % 64) return false;
+  return true;
+}
+
+void step_scratch_sizes(const DMat* const w0[6], int R, int U, int H, int T, int64_t* part, int64_t* xpart,
+                        int64_t* xmax, int64_t* sync) {
+  const int G = sm_count();
+  int64_t units = 0, groups = 0;
+  for (int m = 0; m < 6; m++) {
+    const MmPlan p = plan_of(*w0[m], G);
+    units = std::max<int64_t>(units, (int64_t)p.groups * p.ks);
+    groups = std::max<int64_t>(groups, p.groups);
+  }
+  const int xc = xchunks_of(U, H, T, G);
+  *part = units * R * 128;
+  *xpart = (int64_t)xc * R * H * 65;
+  *xmax = (int64_t)xc * R * H;
+  *sync = 4 + groups + (int64_t)U * H;
+}
+
+int launch_step(StepArgs a, const DMat* const w0[6], cudaStream_t st) {
+  const int G = sm_count();
+  int groups = 0;
+  for (int m = 0; m < 6; m++) {
+    a.mm[m] = plan_of(*w0[m], G);
+    groups = std::max(groups, a.mm[m].groups);
+  }
+  a.max_groups = groups;
+  a.xchunks = xchunks_of(a.U, a.H, a.T, G);
+  int64_t nsync = 4 + groups + (int64_t)a.U * a.H;
+  if (cudaMemsetAsync(a.sync, 0, (size_t)nsync * 4, st) != cudaSuccess) {
+    set_error("step kernel: clearing the counters failed");
+    return WG_ERR_CUDA;
+  }
+  switch (w0[0]->qtype) {
+    case WG_QTYPE_Q8_0: return launch_step_q<WG_QTYPE_Q8_0>(a, st);
+    case WG_QTYPE_Q4_0: return launch_step_q<WG_QTYPE_Q4_0>(a, st);
+    case WG_QTYPE_Q4_1: return launch_step_q<WG_QTYPE_Q4_1>(a, st);
+    case WG_QTYPE_Q5_0: return launch_step_q<WG_QTYPE_Q5_0>(a, st);
+    default: return launch_step_q<WG_QTYPE_Q5_1>(a, st);
+  }
+}
+
+int init_step_attributes() {
+  int rc = configure_step_t<WG_QTYPE_Q8_0, 1>();
   if (rc == WG_OK) rc = configure_step_t<WG_QTYPE_Q8_0, 2>();
   if (rc == WG_OK) rc = configure_step_t<WG_QTYPE_Q4_0, 1>();
   if (rc == WG_OK) rc = configure_step_t<WG_QTYPE_Q4_0, 2>();
@@ -726,6 +777,15 @@ int step_error_word(int* word, bool clear) {
     cudaMemcpyToSymbol(g_step_error, &z, sizeof(int));
   }
   *word = v;
+  return WG_OK;
+}
+
+int step_error_ptr(int** p) {
+  cudaError_t e = cudaGetSymbolAddress((void**)p, g_step_error);
+  if (e != cudaSuccess) {
+    set_error("step kernel error word: %s", cudaGetErrorString(e));
+    return WG_ERR_CUDA;
+  }
   return WG_OK;
 }
 

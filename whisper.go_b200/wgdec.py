@@ -35,7 +35,7 @@ MODE_CORRECT = 1
 WG_OK = 0
 STATUS = {0: "ok", 1: "invalid", 2: "cuda", 3: "oom", 4: "unsupported", 5: "cancelled", 6: "timeout",
           7: "injected", 8: "no_device", 9: "device_flag"}
-KCLASS = {"gemv": 0, "self_attn": 1, "cross_attn": 2, "logits": 3, "precompute": 4,
+KCLASS = {"gemv": 0, "self_attn": 1, "cross_attn": 2, "logits": 3, "precompute": 4, "step": 5,
           "qkv": 10, "self_out": 11, "cross_q": 12, "cross_out": 13, "mlp0": 14, "mlp2": 15}
 
 c_float_p = ctypes.POINTER(ctypes.c_float)
@@ -116,6 +116,7 @@ def _declare(lib):
         "wg_job_cancel": (ctypes.c_int, [P]),
         "wg_job_timer": (ctypes.c_int, [P, ctypes.c_int, ctypes.POINTER(ctypes.c_double)]),
         "wg_job_destroy": (ctypes.c_int, [P]),
+        "wg_job_uses_step_kernel": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_int)]),
         "wg_job_stats": (ctypes.c_int, [P, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
                                         ctypes.POINTER(ctypes.c_int)]),
         "wg_decode": (ctypes.c_int, [P, ctypes.POINTER(c_float_p), ctypes.c_int, ctypes.c_int, c_int32_p,
@@ -726,6 +727,11 @@ class Job:
         a, b, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
         check(lib().wg_job_stats(self.h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c)))
         return a.value, b.value, c.value
+
+    def uses_step_kernel(self) -> bool:
+        on = ctypes.c_int(0)
+        check(lib().wg_job_uses_step_kernel(self.h, ctypes.byref(on)))
+        return bool(on.value)
 
     def time_kernel(self, kclass: str, iters: int = 5):
         ms, nbytes = ctypes.c_double(), ctypes.c_double()
