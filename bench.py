@@ -65,6 +65,9 @@ def parse():
                          "splitting the GPU's utterances")
     ap.add_argument("--layers", type=int, default=0,
                     help="decoder layers (default: the config's); fewer only for small profiler captures")
+    ap.add_argument("--only-class", default="",
+                    help="profiler captures: start one decode job, launch only this kernel class "
+                         "(wgdec.KCLASS: logits, cross_attn, self_attn, step, ...) --steps times, print nothing else")
     return ap.parse_args()
 
 
@@ -301,6 +304,16 @@ def main():
             t.join()
         if errs:
             raise errs[0]
+
+    if args.only_class:  # one kernel class on its own, for an ncu capture of just its launches
+        jobs[0].start()
+        for _ in range(args.steps):
+            jobs[0].time_kernel(args.only_class, iters=1)
+        for jb in jobs:
+            jb.close()
+        dec.close()
+        dist.close()
+        return 0
 
     def decode_once():
         for jb in jobs:

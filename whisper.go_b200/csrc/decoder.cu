@@ -144,11 +144,11 @@ int64_t env_i64(const char* name, int64_t dflt) {
   return strtoll(v, nullptr, 10);
 }
 
-// WG_STEP_KERNEL=0 keeps every small-batch step on the separate kernels
-// (read at every forward pass, so a test can compare both in one process).
+// WG_STEP_KERNEL=1 runs the layers of small-batch jobs as the persistent
+// step kernel (step.cu); read at job creation and at every forward pass.
 bool env_step_enabled() {
   const char* v = getenv("WG_STEP_KERNEL");
-  return !(v && v[0] == '0');
+  return v && v[0] == '1';
 }
 
 // Waits for a stream with the host watchdog deadline (WG_TIMEOUT_MS).

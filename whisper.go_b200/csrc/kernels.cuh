@@ -155,7 +155,8 @@ struct StepArgs {
   int* err;                    // the step kernel's error word (step_error_word)
 };
 // Whether the step kernel can run this model at R rows (weights of one
-// quantised type, K % 64 == 0, head dim 64, R <= 16; WG_STEP_KERNEL=0: never).
+// quantised type, K % 64 == 0, head dim 64, R <= 16) and is switched on
+// (WG_STEP_KERNEL=1; off by default: measured slower than the kernel chain).
 bool step_supported(const DMat* const w0[6], int R, int hd, int d, int T, int Tmax);
 // Scratch of a job using the step kernel: floats of part / xpart / xmax and
 // unsigned of sync.

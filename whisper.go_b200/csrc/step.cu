@@ -54,6 +54,8 @@ constexpr int ST_MAX_ROWS = 16;
 constexpr int ST_MAX_CHUNKS = 8;  // frame chunks of one cross-attention head
 constexpr int ST_MAX_POS = 448;   // KV positions (n_text_ctx)
 constexpr int ST_MAX_FRAMES_CHUNK = 256;
+constexpr int ST_MAX_SPLITS = 16;  // K splits of one matmul
+constexpr int ST_VBATCH = 8;       // V rows in flight per warp (attention)
 
 // ---------------------------------------------------------------------------
 // synchronisation (all waits bounded: 2 s of %globaltimer)
@@ -167,19 +169,35 @@ __device__ void ring_issue(const StepArgs& a, Ring& rg) {
 // ---------------------------------------------------------------------------
 // activations of a matmul unit
 // ---------------------------------------------------------------------------
-// Row statistics of LayerNorm (ops.go:153-202) for all rows: mean, std.
+// Row statistics of LayerNorm (ops.go:153-202) for all rows: mean, std; one
+// warp per row held in registers as float4 runs (d = 128 nv, nv <= 10), all
+// loads in flight at once (the layernorm_reg_kernel arithmetic).
+constexpr int ST_LN_NV = 10;
 __device__ void ln_stats(const StepArgs& a, float* stat) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nv = a.d >> 7;
   for (int r = warp; r < a.R; r += ST_WARPS) {
-    const float* xr = a.x + (int64_t)r * a.d;
+    const float4* x4 = reinterpret_cast<const float4*>(a.x + (int64_t)r * a.d);
+    float4 v[ST_LN_NV];
+#pragma unroll
+    for (int j = 0; j < ST_LN_NV; j++)
+      if (j < nv) v[j] = __ldcg(x4 + lane + 32 * j);
     float s = 0.f;
-    for (int i = lane; i < a.d; i += 32) s += __ldcg(xr + i);
+#pragma unroll
+    for (int j = 0; j < ST_LN_NV; j++)
+      if (j < nv) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
     s = warp_sum(s);
     const float mean = __fdiv_rn(s, (float)a.d);
     float q = 0.f;
-    for (int i = lane; i < a.d; i += 32) {
-      const float dd = __fsub_rn(__ldcg(xr + i), mean);
-      q = __fmaf_rn(dd, dd, q);
+#pragma unroll
+    for (int j = 0; j < ST_LN_NV; j++) {
+      if (j < nv) {
+        const float e0 = __fsub_rn(v[j].x, mean), e1 = __fsub_rn(v[j].y, mean), e2 = __fsub_rn(v[j].z, mean),
+                    e3 = __fsub_rn(v[j].w, mean);
+        q = __fmaf_rn(e0, e0, q);
+        q = __fmaf_rn(e1, e1, q);
+        q = __fmaf_rn(e2, e2, q);
+        q = __fmaf_rn(e3, e3, q);
+      }
     }
     q = warp_sum(q);
     if (lane == 0) {
@@ -193,34 +211,81 @@ enum Src { SRC_LN = 0, SRC_ATT = 1, SRC_CROSS = 2, SRC_H = 3 };
 
 // Stages rows [0, RC) x columns [k0, k0 + kn) of the unit's input as f16
 // high + (scaled) low parts: x_hi = f16(v), x_lo = f16((v - x_hi) * 2^10).
+// Four adjacent columns per item; the loads of all of a thread's items are
+// issued before any is used (a phase is a short, latency-bound step).
+constexpr int ST_STAGE_ITEMS = 4;  // items per thread in one batch
 __device__ void stage_x(const StepArgs& a, int src, const float* lnw, const float* lnb, const float* stat, int k0,
                         int kn, int RC, int stride, __half* xh, __half* xl) {
-  const int width = src == SRC_H ? 4 * a.d : a.d;
-  for (int i = threadIdx.x; i < RC * kn; i += blockDim.x) {
-    const int r = i / kn, kk = i - r * kn, k = k0 + kk;
-    float v = 0.f;
-    if (r < a.R) {
-      if (src == SRC_LN) {
-        const float xv = __ldcg(a.x + (int64_t)r * a.d + k);
-        v = __fadd_rn(__fdiv_rn(__fmul_rn(lnw[k], __fsub_rn(xv, stat[2 * r])), stat[2 * r + 1]), lnb[k]);
-      } else if (src == SRC_ATT) {
-        v = __ldcg(a.att + (int64_t)r * a.d + k);
-      } else if (src == SRC_H) {
-        v = __ldcg(a.h + (int64_t)r * width + k);
-      } else {  // cross-attention: combine the frame chunks of (row, head)
-        const int hh = k >> 6, c = k & 63;
-        float o = 0.f, l = 0.f;
-        for (int ch = 0; ch < a.xchunks; ch++) {
-          const float* p = a.xpart + (((int64_t)ch * a.R + r) * a.H + hh) * 65;
-          o += __ldcg(p + c);
-          l += __ldcg(p + 64);
+  const int kq = kn >> 2, items = a.R * kq;
+  for (int base = threadIdx.x; base < items; base += ST_STAGE_ITEMS * blockDim.x) {
+    float4 v[ST_STAGE_ITEMS];
+#pragma unroll
+    for (int it = 0; it < ST_STAGE_ITEMS; it++) {
+      const int i = base + it * blockDim.x;
+      v[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i >= items) continue;
+      const int r = i / kq, k = k0 + 4 * (i - r * kq);
+      if (src == SRC_LN || src == SRC_ATT) v[it] = __ldcg(reinterpret_cast<const float4*>((src == SRC_LN ? a.x : a.att) + (int64_t)r * a.d + k));
+      else if (src == SRC_H) v[it] = __ldcg(reinterpret_cast<const float4*>(a.h + (int64_t)r * 4 * a.d + k));
+    }
+    if (src == SRC_CROSS) {  // combine the frame chunks of (row, head): o / l
+      for (int it = 0; it < ST_STAGE_ITEMS; it++) {
+        const int i = base + it * blockDim.x;
+        if (i >= items) continue;
+        const int r = i / kq, k = k0 + 4 * (i - r * kq), hh = k >> 6, c = k & 63;
+        float4 o[ST_MAX_CHUNKS];
+        float l[ST_MAX_CHUNKS];
+#pragma unroll
+        for (int ch = 0; ch < ST_MAX_CHUNKS; ch++) {
+          if (ch < a.xchunks) {
+            const float* p = a.xpart + (((int64_t)ch * a.R + r) * a.H + hh) * 68;
+            o[ch] = __ldcg(reinterpret_cast<const float4*>(p + c));
+            l[ch] = __ldcg(p + 64);
+          }
         }
-        v = __fmul_rn(o, __fdiv_rn(1.0f, l));
+        float4 so = make_float4(0.f, 0.f, 0.f, 0.f);
+        float sl = 0.f;
+#pragma unroll
+        for (int ch = 0; ch < ST_MAX_CHUNKS; ch++) {
+          if (ch < a.xchunks) {
+            so.x += o[ch].x; so.y += o[ch].y; so.z += o[ch].z; so.w += o[ch].w;
+            sl += l[ch];
+          }
+        }
+        const float inv = __fdiv_rn(1.0f, sl);
+        v[it] = make_float4(__fmul_rn(so.x, inv), __fmul_rn(so.y, inv), __fmul_rn(so.z, inv), __fmul_rn(so.w, inv));
       }
     }
-    const __half hv = __float2half_rn(v);
-    xh[r * stride + kk] = hv;
-    xl[r * stride + kk] = __float2half_rn(__fmul_rn(__fsub_rn(v, __half2float(hv)), SPLIT_SCALE));
+#pragma unroll
+    for (int it = 0; it < ST_STAGE_ITEMS; it++) {
+      const int i = base + it * blockDim.x;
+      if (i >= items) continue;
+      const int r = i / kq, kk = 4 * (i - r * kq), k = k0 + kk;
+      float f[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
+      if (src == SRC_LN) {
+        const float4 w = *reinterpret_cast<const float4*>(lnw + k), b = *reinterpret_cast<const float4*>(lnb + k);
+        const float ww[4] = {w.x, w.y, w.z, w.w}, bb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++)
+          f[e] = __fadd_rn(__fdiv_rn(__fmul_rn(ww[e], __fsub_rn(f[e], stat[2 * r])), stat[2 * r + 1]), bb[e]);
+      }
+      __half hv[4], lv[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        hv[e] = __float2half_rn(f[e]);
+        lv[e] = __float2half_rn(__fmul_rn(__fsub_rn(f[e], __half2float(hv[e])), SPLIT_SCALE));
+      }
+      *reinterpret_cast<uint2*>(xh + r * stride + kk) =
+          make_uint2(h2_as_u32(__halves2half2(hv[0], hv[1])), h2_as_u32(__halves2half2(hv[2], hv[3])));
+      *reinterpret_cast<uint2*>(xl + r * stride + kk) =
+          make_uint2(h2_as_u32(__halves2half2(lv[0], lv[1])), h2_as_u32(__halves2half2(lv[2], lv[3])));
+    }
+  }
+  // rows R..RC-1 of the MMA tile: zero
+  for (int i = threadIdx.x; i < (RC - a.R) * (kn >> 2); i += blockDim.x) {
+    const int r = a.R + i / (kn >> 2), kk = 4 * (i % (kn >> 2));
+    *reinterpret_cast<uint2*>(xh + r * stride + kk) = make_uint2(0, 0);
+    *reinterpret_cast<uint2*>(xl + r * stride + kk) = make_uint2(0, 0);
   }
 }
 
@@ -319,8 +384,14 @@ __device__ void mm_unit(const StepArgs& a, const UnitRef& ur, const unsigned cha
   for (int i = threadIdx.x; i < a.R * 128; i += blockDim.x) {
     const int r = i >> 7, row = i & 127, n = ur.g * 128 + row;
     if (n >= N) continue;
+    float pv[ST_MAX_SPLITS];  // every split's partial loaded before the ordered sum
+#pragma unroll
+    for (int kz = 0; kz < ST_MAX_SPLITS; kz++)
+      pv[kz] = kz < pl.ks ? __ldcg(base + ((int64_t)kz * a.R + r) * 128 + row) : 0.f;
     float v = 0.f;
-    for (int kz = 0; kz < pl.ks; kz++) v += __ldcg(base + ((int64_t)kz * a.R + r) * 128 + row);  // in split order
+#pragma unroll
+    for (int kz = 0; kz < ST_MAX_SPLITS; kz++)
+      if (kz < pl.ks) v += pv[kz];  // in split order
     switch (ur.m) {
       case 0: {  // q | k | v (decoder.go:840-870); K and V of this position into the cache
         const int seg = n / a.d, j = n - seg * a.d, hh = j >> 6, c = j & 63;
@@ -437,14 +508,26 @@ __device__ void self_attn_unit(const StepArgs& a, int l, int r, int hh, float* s
   s = 0.f;
   for (int w = 0; w < ST_WARPS; w++) s += red[ST_WARPS * 64 + w];
   const float inv = __fdiv_rn(1.0f, s);  // s >= 1: the maximum's weight is exactly 1
-  // out = weights . V: warp per position, lane per channel pair
+  // out = weights . V: warp per position, lane per channel pair, the V rows
+  // of ST_VBATCH positions loaded before use
   float o0 = 0.f, o1 = 0.f;
-  for (int tt = warp; tt < n; tt += ST_WARPS) {
-    const __half2 v = __ldcg(reinterpret_cast<const __half2*>(kvl + (slab(tt) + (int64_t)a.H * a.Tmax + tt) * 64) + lane);
-    const float w = __fmul_rn(sc[tt], inv);
-    const float2 f = __half22float2(v);
-    o0 = fmaf(w, f.x, o0);
-    o1 = fmaf(w, f.y, o1);
+  for (int t0 = warp; t0 < n; t0 += ST_WARPS * ST_VBATCH) {
+    __half2 vv[ST_VBATCH];
+#pragma unroll
+    for (int j = 0; j < ST_VBATCH; j++) {
+      const int tt = t0 + j * ST_WARPS;
+      vv[j] = tt < n ? __ldcg(reinterpret_cast<const __half2*>(kvl + (slab(tt) + (int64_t)a.H * a.Tmax + tt) * 64) + lane)
+                     : __float2half2_rn(0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < ST_VBATCH; j++) {
+      const int tt = t0 + j * ST_WARPS;
+      if (tt >= n) continue;
+      const float w = __fmul_rn(sc[tt], inv);
+      const float2 f = __half22float2(vv[j]);
+      o0 = fmaf(w, f.x, o0);
+      o1 = fmaf(w, f.y, o1);
+    }
   }
   red[warp * 64 + 2 * lane] = o0;
   red[warp * 64 + 2 * lane + 1] = o1;
@@ -525,15 +608,26 @@ __device__ void cross_attn_unit(const StepArgs& a, int l, int u, int hh, int ch,
   float o[ST_MAX_ROWS][2];
 #pragma unroll
   for (int b = 0; b < ST_MAX_ROWS; b++) o[b][0] = o[b][1] = 0.f;
-  for (int i = warp; i < nt; i += ST_WARPS) {
-    const float2 f = __half22float2(reinterpret_cast<const __half2*>(vb + (int64_t)(t0 + i) * 64)[lane]);
+  for (int i0 = warp; i0 < nt; i0 += ST_WARPS * ST_VBATCH) {
+    __half2 vv[ST_VBATCH];
 #pragma unroll
-    for (int b = 0; b < ST_MAX_ROWS; b++)
-      if (b < B) {
-        const float e = sc[b * ST_MAX_FRAMES_CHUNK + i];
-        o[b][0] = fmaf(e, f.x, o[b][0]);
-        o[b][1] = fmaf(e, f.y, o[b][1]);
-      }
+    for (int j = 0; j < ST_VBATCH; j++) {
+      const int i = i0 + j * ST_WARPS;
+      vv[j] = i < nt ? reinterpret_cast<const __half2*>(vb + (int64_t)(t0 + i) * 64)[lane] : __float2half2_rn(0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < ST_VBATCH; j++) {
+      const int i = i0 + j * ST_WARPS;
+      if (i >= nt) continue;
+      const float2 f = __half22float2(vv[j]);
+#pragma unroll
+      for (int b = 0; b < ST_MAX_ROWS; b++)
+        if (b < B) {
+          const float e = sc[b * ST_MAX_FRAMES_CHUNK + i];
+          o[b][0] = fmaf(e, f.x, o[b][0]);
+          o[b][1] = fmaf(e, f.y, o[b][1]);
+        }
+    }
   }
 #pragma unroll
   for (int b = 0; b < ST_MAX_ROWS; b++)
@@ -542,15 +636,18 @@ __device__ void cross_attn_unit(const StepArgs& a, int l, int u, int hh, int ch,
       red[(warp * ST_MAX_ROWS + b) * 64 + 2 * lane + 1] = o[b][1];
     }
   __syncthreads();
-  for (int i = threadIdx.x; i < B * 65; i += blockDim.x) {
-    const int b = i / 65, c = i - b * 65;
+  for (int i = threadIdx.x; i < B * 64; i += blockDim.x) {
+    const int b = i >> 6, c = i & 63;
     float v = 0.f;
-    if (c < 64) {
-      for (int w = 0; w < ST_WARPS; w++) v += red[(w * ST_MAX_ROWS + b) * 64 + c];
-    } else {
-      for (int j = 0; j < nt; j++) v += sc[b * ST_MAX_FRAMES_CHUNK + j];
-    }
-    a.xpart[(((int64_t)ch * a.R + u * B + b) * a.H + hh) * 65 + c] = v;
+#pragma unroll
+    for (int w = 0; w < ST_WARPS; w++) v += red[(w * ST_MAX_ROWS + b) * 64 + c];
+    a.xpart[(((int64_t)ch * a.R + u * B + b) * a.H + hh) * 68 + c] = v;
+  }
+  for (int b = warp; b < B; b += ST_WARPS) {  // l = sum of the chunk's weights, one warp per row
+    float l = 0.f;
+    for (int j = lane; j < nt; j += 32) l += sc[b * ST_MAX_FRAMES_CHUNK + j];
+    l = warp_sum(l);
+    if (lane == 0) a.xpart[(((int64_t)ch * a.R + u * B + b) * a.H + hh) * 68 + 64] = l;
   }
   __syncthreads();
 }
@@ -660,7 +757,7 @@ MmPlan plan_of(const DMat& W, int G) {
   p.per = (p.pairs + ks - 1) / ks;
   if (p.per > ST_MAX_PAIRS) p.per = ST_MAX_PAIRS;
   p.ks = (p.pairs + p.per - 1) / p.per;
-  return p;
+  return p;  // ks <= ST_MAX_SPLITS: step_supported checks it
 }
 
 int xchunks_of(int U, int H, int T, int G) {
@@ -700,15 +797,18 @@ int launch_step_q(const StepArgs& a, cudaStream_t st) {
 
 bool step_supported(const DMat* const w0[6], int R, int hd, int d, int T, int Tmax) {
   static int on = -1;
-  if (on < 0) {
+  if (on < 0) {  // opt-in (WG_STEP_KERNEL=1): measured slower than the kernel chain
     const char* v = getenv("WG_STEP_KERNEL");
-    on = !(v && v[0] == '0');
+    on = v && v[0] == '1';
   }
   if (!on || R < 1 || R > ST_MAX_ROWS || hd != 64 || d % 64 || T < 1 || Tmax > ST_MAX_POS ||
       (T + ST_MAX_FRAMES_CHUNK - 1) / ST_MAX_FRAMES_CHUNK > ST_MAX_CHUNKS || T > 4 * 1024)
     return false;
-  for (int m = 0; m < 6; m++)
+  if (d % 128 || d / 128 > ST_LN_NV) return false;  // LayerNorm rows in registers
+  for (int m = 0; m < 6; m++) {
     if (!qtype_is_quant(w0[m]->qtype) || w0[m]->qtype != w0[0]->qtype || w0[m]->cols % 64) return false;
+    if (plan_of(*w0[m], sm_count()).ks > ST_MAX_SPLITS) return false;
+  }
   return true;
 }
 
@@ -723,7 +823,7 @@ void step_scratch_sizes(const DMat* const w0[6], int R, int U, int H, int T, int
   }
   const int xc = xchunks_of(U, H, T, G);
   *part = units * R * 128;
-  *xpart = (int64_t)xc * R * H * 65;
+  *xpart = (int64_t)xc * R * H * 68;
   *xmax = (int64_t)xc * R * H;
   *sync = 4 + groups + (int64_t)U * H;
 }
