@@ -154,14 +154,14 @@ def test_cancel_during_decode(tiny):
 
 @pytest.mark.parametrize("qtype", ["Q4_0", "Q4_1", "Q5_0", "Q5_1", "Q8_0"])
 def test_teacher_forced_tensor_core_path(qtype):
-    """20 utterances (R = 20 > 16): every GEMM of the step, the cross K/V
-    precompute and the logits run on the tcgen05 kernel (dequantised tiles
-    in tensor memory), with all epilogue modes (QKV scatter, residual add,
-    GELU, cross K/V scatter), for each quantisation type."""
+    """50 utterances (R = 50 > 16): every GEMM of the step, the cross K/V
+    precompute and the logits run on the tcgen05 kernel (dequantised tiles in
+    tensor memory), with all epilogue modes (QKV scatter, residual add, GELU,
+    cross K/V scatter), for each quantisation type."""
     m = wgdec.SyntheticModel(51864, 256, 4, 2, 448, qtype, seed=23)
     dec = wgdec.WhisperDecoder(m)
     try:
-        U, T = 20, 64
+        U, T = 50, 64
         encs = [m.encoder_output(u, T) for u in range(U)]
         forced = np.random.default_rng(5).integers(0, 50257, size=(U, 3))
         gpu = dec.teacher_forced_logits(encs, PROMPT, forced, wgdec.MODE_CORRECT)

@@ -92,11 +92,12 @@ def test_matmul_tcgen05_model_shapes(R, rows, K):
 
 @pytest.mark.parametrize("qt", ["Q8_0", "Q5_1"])
 @pytest.mark.parametrize("R,rows,K", [(5, 1280, 5120), (1, 3840, 1280), (16, 5120, 1280), (5, 1300, 1280),
-                                      (3, 2000, 768)])
+                                      (3, 2000, 768), (24, 1280, 1280), (40, 3840, 1280), (40, 1280, 5120),
+                                      (48, 5120, 1280), (33, 1300, 768)])
 def test_matmul_small_batch_model_shapes(qt, R, rows, K):
     """The small-batch GEMV (path 1: a 128-row weight group per CTA, K ranges
-    summed across a thread-block cluster) at decoder shapes, with partial
-    weight groups and K split into up to 8 ranges."""
+    summed across a thread-block cluster) at decoder shapes up to 48 rows,
+    with partial weight groups and K split into up to 16 ranges."""
     raw, a, ref = _matmul_case(qt, R, rows, K, seed=R + rows + K)
     gpu = wgdec.matmul(qt, raw, rows, K, a, path=1)
     assert _close(gpu, ref), float(np.max(np.abs(gpu - ref)))

@@ -7,8 +7,8 @@ file runs the kernels the benchmark itself runs, against the CPU oracle:
   configuration (configs 1-4 in full; config 5, large-v3-shaped, with 4 of
   its 32 layers), 200 forced tokens so the f16 KV cache is read out to
   position 203 (the bench decodes positions 3..227);
-* batched teacher forcing at config 5 / config 4 widths with 32 and 40 rows
-  per step (tcgen05 GEMMs, the 4-warp self-attention kernel from 512
+* batched teacher forcing at config 5 / config 4 widths with 32, 40 and 56
+  rows per step (tcgen05 GEMMs, the 4-warp self-attention kernel from 512
   (row, head) pairs on, the streaming cross-attention kernel);
 * greedy decoding with 72 rows (the one-CTA-per-row greedy kernel above 64
   rows) and beam-5 decoding of 14 utterances (70 rows: the one-CTA top-k
@@ -113,13 +113,15 @@ def test_teacher_forced_ref_compat_config_shape():
         m.close()
 
 
-@pytest.mark.parametrize("name,U,n,check", [("c5", 32, 48, (0, 13, 31)), ("c4", 40, 24, (0, 39))])
+@pytest.mark.parametrize("name,U,n,check", [("c5", 32, 48, (0, 13, 31)), ("c4", 40, 24, (0, 39)),
+                                             ("c5", 56, 24, (0, 55))])
 def test_teacher_forced_batched_rows(name, U, n, check):
     """U rows per step at config 5 / config 4 widths: every matmul on the
-    tcgen05 kernel, self-attention on the 4-warp kernel (R * H >= 512),
-    cross-attention on the streaming kernel (U * H >= 64), LayerNorm kernels
-    between them. All U rows run on the GPU; a few are checked against the
-    oracle (each costs a full CPU decode)."""
+    tcgen05 kernel with LayerNorm kernels between (the small-batch GEMV takes
+    at most 16 rows by default); self-attention on the 4-warp kernel (R * H >= 512),
+    cross-attention on the streaming kernel (U * H >= 64). All U rows run on
+    the GPU; a few are checked against the oracle (each costs a full CPU
+    decode)."""
     m = synthetic(name, layers=4 if name == "c5" else None)
     dec = wgdec.WhisperDecoder(m)
     try:

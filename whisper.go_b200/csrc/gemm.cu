@@ -300,7 +300,7 @@ int large_path_override() {
 template <uint32_t QT>
 int launch_q(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st, int path) {
   if (path == 0) {
-    path = R <= 16 ? 1 : (tc_supported(W) ? 3 : 2);
+    path = (R <= 16 || gemv_bulk_supported(W, R)) ? 1 : (tc_supported(W) ? 3 : 2);
     if (path == 3 && large_path_override() == 2) path = 2;
   }
   if (path == 1 && gemv_bulk_supported(W, R) && small_path_override() != 4) return launch_gemv_bulk(W, X, ldx, R, e, st);
@@ -350,7 +350,7 @@ bool matmul_fuses_input_ln(const DMat& W, int R) {
     const char* s = getenv("WG_LN_FUSE");
     v = (s && *s) ? atoi(s) : 1;
   }
-  return v != 0 && R <= 16 && gemv_bulk_supported(W, R) && small_path_override() != 4;
+  return v != 0 && gemv_bulk_supported(W, R) && small_path_override() != 4;
 }
 
 int launch_matmul(const DMat& W, const __half* X, int ldx, int R, const Epi& e_in, cudaStream_t st, int path) {

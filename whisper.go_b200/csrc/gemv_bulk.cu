@@ -30,6 +30,10 @@ namespace {
 
 constexpr int GB_WARPS = 8;          // one per 16-row tile of the group
 constexpr int GB_MAX_PAIRS = 12;     // 64-wide K chunks per CTA (shared memory bound)
+constexpr int GB_MAX_NB = 6;         // 8-row activation blocks: up to 48 rows per step
+// K chunks per CTA for NB activation blocks: the activation rows (f16 high +
+// low parts) grow with NB, so wider batches take shorter K ranges
+__host__ __device__ constexpr int gb_max_pairs(int NB) { return NB <= 2 ? GB_MAX_PAIRS : 8; }
 constexpr int GB_MAX_CLUSTER = 16;   // K ranges per group (non-portable cluster size)
 constexpr int GB_TARGET_CTAS = 296;  // two per SM
 
@@ -295,7 +299,7 @@ int launch_gb_t(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cu
   }
   int kc = std::min(max_kc, std::max(1, (GB_TARGET_CTAS + groups - 1) / groups));
   int per = (pairs + kc - 1) / kc;
-  if (per > GB_MAX_PAIRS) per = GB_MAX_PAIRS;
+  if (per > gb_max_pairs(NB)) per = gb_max_pairs(NB);
   kc = (pairs + per - 1) / per;
   if (kc > max_kc) {
     set_error("gemv_bulk: K=%d needs more than %d K ranges", W.cols, GB_MAX_CLUSTER);
@@ -322,7 +326,14 @@ int launch_gb_t(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cu
 
 template <uint32_t QT>
 int launch_gb_q(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st) {
-  return R <= 8 ? launch_gb_t<QT, 1>(W, X, ldx, R, e, st) : launch_gb_t<QT, 2>(W, X, ldx, R, e, st);
+  switch ((R + 7) / 8) {
+    case 1: return launch_gb_t<QT, 1>(W, X, ldx, R, e, st);
+    case 2: return launch_gb_t<QT, 2>(W, X, ldx, R, e, st);
+    case 3: return launch_gb_t<QT, 3>(W, X, ldx, R, e, st);
+    case 4: return launch_gb_t<QT, 4>(W, X, ldx, R, e, st);
+    case 5: return launch_gb_t<QT, 5>(W, X, ldx, R, e, st);
+    default: return launch_gb_t<QT, 6>(W, X, ldx, R, e, st);
+  }
 }
 
 template <uint32_t QT, int NB>
@@ -341,14 +352,37 @@ int configure_gb_t() {
 template <uint32_t QT>
 int configure_gb_q() {
   int rc = configure_gb_t<QT, 1>();
-  return rc == WG_OK ? configure_gb_t<QT, 2>() : rc;
+  if (rc == WG_OK) rc = configure_gb_t<QT, 2>();
+  if (rc == WG_OK) rc = configure_gb_t<QT, 3>();
+  if (rc == WG_OK) rc = configure_gb_t<QT, 4>();
+  if (rc == WG_OK) rc = configure_gb_t<QT, 5>();
+  if (rc == WG_OK) rc = configure_gb_t<QT, 6>();
+  return rc;
 }
 
 }  // namespace
 
+// Rows per step up to which the small-batch GEMV takes a matmul (with its
+// fused LayerNorm) instead of the tcgen05 GEMM: WG_GEMV_MAX_ROWS (at most
+// 48), default 16. Measured at 40 rows (large-v3, 8 utterances x beam 5):
+// 13.4 us per launch against 7.3 us on the tcgen05 GEMM, the three
+// mma.sync products of the split operands for 5 row blocks outweighing the
+// saved LayerNorm kernels.
+int gemv_bulk_max_rows() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("WG_GEMV_MAX_ROWS");
+    v = (s && *s) ? atoi(s) : 16;
+    if (v < 1) v = 1;
+    if (v > 8 * GB_MAX_NB) v = 8 * GB_MAX_NB;
+  }
+  return v;
+}
+
 bool gemv_bulk_supported(const DMat& W, int R) {
-  return R >= 1 && R <= 16 && qtype_is_quant(W.qtype) && W.cols % 64 == 0 &&
-         (W.kblocks / 2 + GB_MAX_PAIRS - 1) / GB_MAX_PAIRS <= 8;
+  const int NB = (R + 7) / 8;
+  return R >= 1 && R <= gemv_bulk_max_rows() && qtype_is_quant(W.qtype) && W.cols % 64 == 0 &&
+         (W.kblocks / 2 + gb_max_pairs(NB) - 1) / gb_max_pairs(NB) <= GB_MAX_CLUSTER;
 }
 
 int launch_gemv_bulk(const DMat& W, const __half* X, int ldx, int R, const Epi& e, cudaStream_t st) {

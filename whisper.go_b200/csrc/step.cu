@@ -753,7 +753,7 @@ MmPlan plan_of(const DMat& W, int G) {
   MmPlan p;
   p.groups = (W.ntiles + 7) / 8;
   p.pairs = W.kblocks / 2;
-  int ks = std::max(1, std::min(p.pairs, (G + p.groups / 2) / p.groups));
+  int ks = std::max(1, std::min(std::min(p.pairs, ST_MAX_SPLITS), (G + p.groups / 2) / p.groups));
   p.per = (p.pairs + ks - 1) / ks;
   if (p.per > ST_MAX_PAIRS) p.per = ST_MAX_PAIRS;
   p.ks = (p.pairs + p.per - 1) / p.per;
