@@ -190,9 +190,14 @@ class Clocks:
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of each kernel class
-# on the default workload, from the ncu captures summarised under profiles/
-# (None where no capture covers the class)
-TRAFFIC = {"gemv": 6.19e6, "cross_attn": 500.6e6, "self_attn": 375.8e6}
+# on the default workload (config 5, 64 utterances per GPU, 32 layers), taken
+# from one ncu capture each, not measured in every run:
+#   gemv       mean of the six token-loop GEMM shapes, profiles/gemm_tc_large_v3.md
+#   cross_attn profiles/cross_attn_stream_large_v3.md
+#   self_attn  profiles/attn_simt_self_large_v3.md
+#   logits     profiles/logits_gemm_large_v3.md
+# Other workloads report None (no capture covers them).
+TRAFFIC = {"gemv": 6.19e6, "cross_attn": 500.6e6, "self_attn": 375.8e6, "logits": 154.7e6}
 
 
 def peaks():
@@ -368,9 +373,12 @@ def main():
         classes[k] = {"ms_per_launch": t, "bytes_per_launch": b, "gbs": b / (t * 1e6) if t > 0 else None,
                       "ms_per_step": t * (cfg["L"] if k != "precompute" else 1.0 / max(steps_done, 1))}
     dom = max(main, key=lambda k: classes[k]["ms_per_step"])
+    default_workload = (args.config == 5 and len(ids) == 64 and cfg["L"] == CONFIGS[5]["L"] and not step_kernel
+                        and args.tokens == STEPS_PER_DECODE)
     dk = classes[dom]
     roofline = {"bound": "hbm", "kernel": dom, "achieved": dk["gbs"], "peak": peak, "unit": "GB/s",
-                "frac": dk["gbs"] / peak if dk["gbs"] else None, "traffic": TRAFFIC.get(dom),
+                "frac": dk["gbs"] / peak if dk["gbs"] else None,
+                "traffic": TRAFFIC.get(dom) if default_workload else None,
                 "peak_kind": peak_kind, "classes": classes}
     # the north star's step roofline: quantised weight + KV bytes of one token
     # step (averaged over the decode) at 8 TB/s, against the measured step time

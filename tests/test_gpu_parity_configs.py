@@ -26,8 +26,8 @@ step by step; where they first differ, the oracle's margin at that step must
 be <= 2e-2 (a near-tie the tolerance allows either way), and the comparison
 of that utterance ends there. The margin is the top-2 logit gap for greedy;
 for beam search the smallest of every live row's 5th/6th logit gap and the
-gaps among the best B+1 candidates' normalised scores (SURVEY gate 4: the
-5th/6th candidate boundary, and the order of the kept beams).
+gaps among the best B+1 candidates' normalised scores (the 5th/6th
+candidate boundary, and the order of the kept beams).
 """
 import os
 

@@ -736,10 +736,9 @@ __global__ void __launch_bounds__(128) beam_update_kernel(SampleState s) {
   if (s.utt_done[u]) return;
   const int B = s.B;
   __shared__ float c_norm[MAXB * TOPK], c_score[MAXB * TOPK], c_lp[MAXB * TOPK];
-  __shared__ int c_parent[MAXB * TOPK], c_tok[MAXB * TOPK], c_carried[MAXB * TOPK];
+  __shared__ int c_parent[MAXB * TOPK], c_tok[MAXB * TOPK];
   __shared__ int nc_sh;
   __shared__ int sel[MAXB];
-  __shared__ int stop_sh;
   if (threadIdx.x == 0) {
     int nc = 0;
     for (int b = 0; b < B; b++) {
@@ -748,7 +747,7 @@ __global__ void __launch_bounds__(128) beam_update_kernel(SampleState s) {
       const int* h = s.hist + (int64_t)r * s.Tcap;
       float sc = s.score[r];
       if (n > 0 && h[n - 1] == s.eot) {
-        c_parent[nc] = b; c_score[nc] = sc; c_tok[nc] = s.eot; c_lp[nc] = 0.f; c_carried[nc] = 1;
+        c_parent[nc] = b; c_score[nc] = sc; c_tok[nc] = s.eot; c_lp[nc] = 0.f;
         c_norm[nc] = __fdiv_rn(sc, (float)pow((double)n, 0.6));
         nc++;
         continue;
@@ -759,7 +758,7 @@ __global__ void __launch_bounds__(128) beam_update_kernel(SampleState s) {
         if (tk < 0) continue;
         float lp = s.topk_lp[r * TOPK + j];
         float ns = __fadd_rn(sc, lp);
-        c_parent[nc] = b; c_score[nc] = ns; c_tok[nc] = tk; c_lp[nc] = lp; c_carried[nc] = 0;
+        c_parent[nc] = b; c_score[nc] = ns; c_tok[nc] = tk; c_lp[nc] = lp;
         c_norm[nc] = __fdiv_rn(ns, den);
         nc++;
       }
@@ -836,7 +835,6 @@ __global__ void __launch_bounds__(128) beam_update_kernel(SampleState s) {
       }
     }
     if (s.utt_steps[u] >= s.max_tokens) stop = true;
-    stop_sh = stop;
     if (stop) {
       s.utt_done[u] = 1;
       atomicAdd(s.n_done, 1);
