@@ -13,7 +13,9 @@
 //    frames; the row maximum and the exponential sum are exchanged through
 //    distributed shared memory so the softmax uses the exact global maximum
 //    like the reference; Q.K^T and P.V run on mma.m16n8k16 (f16 in, f32
-//    accumulate).
+//    accumulate). The exponentials enter P.V unnormalised; the ranks' partial
+//    outputs and exponential sums travel in one exchange and the sum of the
+//    partials is scaled by 1/sum (two cluster exchanges instead of three).
 #include <cooperative_groups.h>
 
 #include "async.cuh"
@@ -307,7 +309,7 @@ __global__ void __launch_bounds__(XA_MAX_WARPS * 32)
   unsigned char* vsm = smem + (size_t)Tc * 128;   // [Tc][64]
   float* stats = reinterpret_cast<float*>(smem + (size_t)Tc * 256);  // [2][16] published to the cluster
   float* wred = stats + 32;                                          // [wpc][16]
-  float* opart = wred + XA_MAX_WARPS * 16;                           // [16][64] CTA partial output
+  float* opart = wred + XA_MAX_WARPS * 16;  // [1 + wpc][16][64]: CTA partial output, then one slot per warp
   const __half* kbase = kvc + ((int64_t)u * 2 * H + h) * (int64_t)T * 64;
   const __half* vbase = kbase + (int64_t)H * T * 64;
   const uint32_t ks_addr = (uint32_t)__cvta_generic_to_shared(ksm);
@@ -405,7 +407,8 @@ __global__ void __launch_bounds__(XA_MAX_WARPS * 32)
     gm0 = fmaxf(gm0, rs[g]);
     gm1 = fmaxf(gm1, rs[g + 8]);
   }
-  // exponentials against the global maximum; partial sums
+  // exponentials against the global maximum, rounded to f16 as the A
+  // fragments of P.V, and this warp's partial sums
   float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
   for (int nb = 0; nb < 8; nb++)
@@ -420,37 +423,20 @@ __global__ void __launch_bounds__(XA_MAX_WARPS * 32)
   sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
   sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
   sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
-  __syncthreads();
+  uint32_t pa[4][4];
+#pragma unroll
+  for (int kk = 0; kk < 4; kk++) {
+    pa[kk][0] = pack_h2(sacc[2 * kk][0], sacc[2 * kk][1]);
+    pa[kk][1] = pack_h2(sacc[2 * kk][2], sacc[2 * kk][3]);
+    pa[kk][2] = pack_h2(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1]);
+    pa[kk][3] = pack_h2(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]);
+  }
+  asm volatile("cp.async.wait_group 0;\n" ::);
+  __syncthreads();  // V in shared memory; every warp is past its reads of wred
   if (t4 == 0) {
     wred[warp * 16 + g] = sum0;
     wred[warp * 16 + g + 8] = sum1;
   }
-  __syncthreads();
-  if (threadIdx.x < 16) {
-    float s = wred[threadIdx.x];
-    for (int w = 1; w < wpc; w++) s += wred[w * 16 + threadIdx.x];
-    stats[16 + threadIdx.x] = s;
-  }
-  cluster.sync();
-  float gs0 = 0.f, gs1 = 0.f;
-  for (int rk = 0; rk < csize; rk++) {
-    const float* rs = cluster.map_shared_rank(stats, rk);
-    gs0 += rs[16 + g];
-    gs1 += rs[16 + g + 8];
-  }
-  const float inv0 = gs0 == 0.f ? 0.f : __fdiv_rn(1.f, gs0);
-  const float inv1 = gs1 == 0.f ? 0.f : __fdiv_rn(1.f, gs1);
-  // weights (e * 1/sum) as f16 A fragments
-  uint32_t pa[4][4];
-#pragma unroll
-  for (int kk = 0; kk < 4; kk++) {
-    pa[kk][0] = pack_h2(__fmul_rn(sacc[2 * kk][0], inv0), __fmul_rn(sacc[2 * kk][1], inv0));
-    pa[kk][1] = pack_h2(__fmul_rn(sacc[2 * kk][2], inv1), __fmul_rn(sacc[2 * kk][3], inv1));
-    pa[kk][2] = pack_h2(__fmul_rn(sacc[2 * kk + 1][0], inv0), __fmul_rn(sacc[2 * kk + 1][1], inv0));
-    pa[kk][3] = pack_h2(__fmul_rn(sacc[2 * kk + 1][2], inv1), __fmul_rn(sacc[2 * kk + 1][3], inv1));
-  }
-  asm volatile("cp.async.wait_group 0;\n" ::);
-  __syncthreads();
   // O = P V over this warp's 64 frames: 8 blocks of 8 dims
   float oacc[8][4];
 #pragma unroll
@@ -470,27 +456,51 @@ __global__ void __launch_bounds__(XA_MAX_WARPS * 32)
       mma16816(oacc[2 * ndp + 1], pa[kk], b[2], b[3]);
     }
   }
-  // CTA partial: warps in order
-  for (int w = 0; w < wpc; w++) {
-    if (warp == w) {
+  // this warp's unnormalised partial output into its slot
+  float* oslot = opart + (1 + warp) * 16 * 64;
 #pragma unroll
-      for (int nd = 0; nd < 8; nd++)
+  for (int nd = 0; nd < 8; nd++)
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-          int row = g + ((c >> 1) << 3), col = nd * 8 + 2 * t4 + (c & 1);
-          float* dst = opart + row * 64 + col;
-          *dst = (w == 0) ? oacc[nd][c] : *dst + oacc[nd][c];
-        }
-    }
-    __syncthreads();
+    for (int c = 0; c < 4; c++) oslot[(g + ((c >> 1) << 3)) * 64 + nd * 8 + 2 * t4 + (c & 1)] = oacc[nd][c];
+  __syncthreads();
+  // the CTA's partial output (slot 0) and exponential sums, warps in order
+  for (int i = threadIdx.x; i < B * 64; i += blockDim.x) {
+    float v = opart[16 * 64 + i];
+    for (int w = 1; w < wpc; w++) v += opart[(1 + w) * 16 * 64 + i];
+    opart[i] = v;
+  }
+  if (threadIdx.x < 16) {
+    float sm = wred[threadIdx.x];
+    for (int w = 1; w < wpc; w++) sm += wred[w * 16 + threadIdx.x];
+    stats[16 + threadIdx.x] = sm;
   }
   cluster.sync();
-  // every rank sums (in rank order) and writes its share of the outputs
+  // every rank takes a share of the outputs: the partial outputs and sums of
+  // all ranks added in rank order, then scaled by 1 / sum (the reference
+  // scales each weight by the same reciprocal before the product)
   for (int i = crank * blockDim.x + threadIdx.x; i < B * 64; i += csize * blockDim.x) {
-    int row = i >> 6, col = i & 63;
-    float v = 0.f;
-    for (int rk = 0; rk < csize; rk++) v += cluster.map_shared_rank(opart, rk)[row * 64 + col];
-    out16[((int64_t)u * B + row) * ldo + h * 64 + col] = __float2half_rn(v);
+    const int row = i >> 6, col = i & 63;
+    float pv[8], ps[8];
+#pragma unroll
+    for (int rk = 0; rk < 8; rk++) {
+      pv[rk] = 0.f;
+      ps[rk] = 0.f;
+      if (rk < csize) {
+        const float* rbase = cluster.map_shared_rank(stats, rk);
+        pv[rk] = cluster.map_shared_rank(opart, rk)[row * 64 + col];
+        ps[rk] = rbase[16 + row];
+      }
+    }
+    float v = 0.f, sm = 0.f;
+#pragma unroll
+    for (int rk = 0; rk < 8; rk++) {
+      if (rk < csize) {
+        v += pv[rk];
+        sm += ps[rk];
+      }
+    }
+    const float inv = sm == 0.f ? 0.f : __fdiv_rn(1.f, sm);
+    out16[((int64_t)u * B + row) * ldo + h * 64 + col] = __float2half_rn(__fmul_rn(v, inv));
   }
   cluster.sync();
 }
@@ -736,7 +746,7 @@ int attn_error_word(int* word, bool clear) {
 
 int init_attn_attributes() {
   cudaError_t e = cudaFuncSetAttribute(cross_attn_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       XA_MAX_WARPS * 64 * 256 + (32 + XA_MAX_WARPS * 16 + 16 * 64) * 4);
+                                       XA_MAX_WARPS * 64 * 256 + (32 + XA_MAX_WARPS * 16 + (1 + XA_MAX_WARPS) * 16 * 64) * 4);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(cross_attn_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)xs_smem());
   if (e != cudaSuccess) {
@@ -805,7 +815,7 @@ int launch_cross_attn(const CrossAttnArgs& c, cudaStream_t st) {
                         "cross_attn_stream");
   }
   int S = (c.T + 64 * wpc - 1) / (64 * wpc);
-  size_t smem = (size_t)wpc * 64 * 256 + (32 + XA_MAX_WARPS * 16 + 16 * 64) * 4;
+  size_t smem = (size_t)wpc * 64 * 256 + (32 + XA_MAX_WARPS * 16 + (size_t)(1 + wpc) * 16 * 64) * 4;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(S, c.H, c.U);
   cfg.blockDim = dim3(32 * wpc, 1, 1);
