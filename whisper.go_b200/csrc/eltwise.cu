@@ -78,16 +78,26 @@ __global__ void layernorm_kernel(const float* __restrict__ x, const float* __res
 }
 
 // Same arithmetic with the row held in registers (d == 128 * NV): one read
-// of x instead of three dependent passes.
+// of x instead of three dependent passes. gamma and beta are model data,
+// never written by the token loop, so each lane loads its share of them
+// before the dependency wait and only the read of x follows it.
 template <int NV>
 __global__ void layernorm_reg_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                      const float* __restrict__ b, int R, __half* __restrict__ out16, int ld16,
                                      float* __restrict__ out32) {
   pdl_trigger();
-  pdl_wait();
   constexpr int d = NV * 128;
   const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+  float4 wv[NV], bw[NV];
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    wv[i] = w4[lane + 32 * i];
+    bw[i] = b4[lane + 32 * i];
+  }
+  pdl_wait();
   if (r >= R) return;
   const float4* xr = reinterpret_cast<const float4*>(x + (int64_t)r * d);
   float4 v[NV];
@@ -110,12 +120,10 @@ __global__ void layernorm_reg_kernel(const float* __restrict__ x, const float* _
   }
   q = warp_sum(q);
   const float sd = __fsqrt_rn(__fadd_rn(__fdiv_rn(q, (float)d), 1e-5f));
-  const float4* w4 = reinterpret_cast<const float4*>(w);
-  const float4* b4 = reinterpret_cast<const float4*>(b);
 #pragma unroll
   for (int i = 0; i < NV; i++) {
     const int c4 = lane + 32 * i;
-    const float4 ww = w4[c4], bv = b4[c4];
+    const float4 ww = wv[i], bv = bw[i];
     float4 o;
     o.x = __fadd_rn(__fdiv_rn(__fmul_rn(ww.x, __fsub_rn(v[i].x, mean)), sd), bv.x);
     o.y = __fadd_rn(__fdiv_rn(__fmul_rn(ww.y, __fsub_rn(v[i].y, mean)), sd), bv.y);

@@ -38,7 +38,7 @@ constexpr int GB_MAX_CLUSTER = 16;   // K ranges per group (non-portable cluster
 constexpr int GB_TARGET_CTAS = 296;  // two per SM
 
 struct GbLayout {
-  uint32_t qs, dsc, msc, hb, xs, xs_lo, red, stat, bar, total;
+  uint32_t qs, dsc, msc, hb, xs, xs_lo, red, stat, lnwb, bar, total;
 };
 
 // Shared-memory layout for np K chunks and RC activation rows.
@@ -55,7 +55,8 @@ __host__ __device__ inline GbLayout gb_layout(uint32_t qt, int np, int RC) {
   L.xs_lo = L.xs + ((uint32_t)RC * xs_stride * 2 + 15) / 16 * 16;
   L.red = L.xs_lo + ((uint32_t)RC * xs_stride * 2 + 15) / 16 * 16;
   L.stat = L.red + 128u * RC * 4;  // [RC][2] LayerNorm mean, std
-  L.bar = L.stat + (uint32_t)RC * 8;
+  L.lnwb = L.stat + (uint32_t)RC * 8;  // LayerNorm gamma, then beta, of the CTA's K range
+  L.bar = L.lnwb + (uint32_t)np * 64 * 4 * 2;
   L.total = L.bar + 16;
   return L;
 }
@@ -150,9 +151,18 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
     if (has_h && lane == 6) bulk_g2s(base + L.hb, W.hb + S0 * 32, slots * 64, bar);
   }
 
+  const int k0 = p0 * 64, kn = np * 64;
+  // LayerNorm gamma / beta of this K range: model data, staged before the wait
+  float4* lnw = reinterpret_cast<float4*>(gb_smem + L.lnwb);
+  float4* lnb = lnw + kn / 4;
+  if (e.ln_x)
+    for (int i = threadIdx.x; i < kn / 4; i += blockDim.x) {
+      lnw[i] = reinterpret_cast<const float4*>(e.ln_w + k0)[i];
+      lnb[i] = reinterpret_cast<const float4*>(e.ln_b + k0)[i];
+    }
+
   // ---- activations of this K range (written by earlier kernels) ----
   pdl_wait();
-  const int k0 = p0 * 64, kn = np * 64;
   const int xs_stride = pairs_per * 64 + 16;
   __half* xsm = reinterpret_cast<__half*>(gb_smem + L.xs);
   __half* xsm_lo = reinterpret_cast<__half*>(gb_smem + L.xs_lo);
@@ -177,8 +187,8 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
       float o[4] = {0.f, 0.f, 0.f, 0.f};
       if (rr < e.R) {
         const float4 x = *reinterpret_cast<const float4*>(e.ln_x + (int64_t)rr * e.ln_d + k);
-        const float4 w = *reinterpret_cast<const float4*>(e.ln_w + k);
-        const float4 b = *reinterpret_cast<const float4*>(e.ln_b + k);
+        const float4 w = lnw[kk / 4];
+        const float4 b = lnb[kk / 4];
         const float mean = stat[2 * rr], sd = stat[2 * rr + 1];
         o[0] = __fadd_rn(__fdiv_rn(__fmul_rn(w.x, __fsub_rn(x.x, mean)), sd), b.x);
         o[1] = __fadd_rn(__fdiv_rn(__fmul_rn(w.y, __fsub_rn(x.y, mean)), sd), b.y);
