@@ -125,7 +125,7 @@ struct TcEpiRow {
   bool ok;
 };
 
-__device__ __forceinline__ TcEpiRow tc_epi_row(const Epi& e, int n) {
+__device__ __forceinline__ TcEpiRow tc_epi_row(const Epi& e, int n, int pos) {
   TcEpiRow er{0, 0, 0.f, n < e.N};
   const int nn = er.ok ? n : 0;
   if (e.mode == EPI_F32 || e.mode == EPI_RESID || e.mode == EPI_GELU_F16) {
@@ -140,7 +140,7 @@ __device__ __forceinline__ TcEpiRow tc_epi_row(const Epi& e, int n) {
       er.row_stride = e.ldo;
     } else {
       er.bias = seg == 2 ? e.bias_v[j] : 0.f;
-      er.col_off = (((int64_t)(seg - 1) * e.H + h) * e.T + *e.pos) * e.hd + c;
+      er.col_off = (((int64_t)(seg - 1) * e.H + h) * e.T + pos) * e.hd + c;
       er.row_stride = (int64_t)2 * e.H * e.T * e.hd;
     }
   } else {  // EPI_CROSS_KV
@@ -548,6 +548,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
   for (int i = 0; i < 4; i++) b4[i] = i < nvalid ? tc_epi_bias(e, n0 + i) : 0.f;
   pdl_wait();  // (returned long ago for the activation loader)
+  // the decode position of the KV-cache scatter, loaded long before the stores
+  const int pos = e.mode == EPI_QKV ? *e.pos : 0;
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = ks > 1 ? (int)cluster.block_rank() : 0;
   const int rows_per = (NR + ks - 1) / ks;
@@ -582,7 +584,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (ks > 1) cluster.sync();
   else __syncthreads();
   if (*abort_flag == 0) {
-    const TcEpiRow er = tc_epi_row(e, n0);
+    const TcEpiRow er = tc_epi_row(e, n0, pos);
     const bool qkv_q = e.mode == EPI_QKV && n0 < e.d;
     // the 4 weight rows are adjacent in the output unless a head of a
     // cache layout ends inside the quad
@@ -607,7 +609,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
       if (!contig) {
         for (int i = 0; i < nvalid; i++)
-          tc_epi_store_run<1>(e, tc_epi_row(e, n0 + i), e.mode == EPI_QKV && n0 + i < e.d, r, R, &a4[i]);
+          tc_epi_store_run<1>(e, tc_epi_row(e, n0 + i, pos), e.mode == EPI_QKV && n0 + i < e.d, r, R, &a4[i]);
         continue;
       }
       float x[4];

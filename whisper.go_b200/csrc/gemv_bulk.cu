@@ -152,6 +152,17 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
   }
 
   const int k0 = p0 * 64, kn = np * 64;
+  // the biases of this thread's first outputs (model data) before the wait
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = kc > 1 ? (int)cluster.block_rank() : 0;
+  constexpr int GB_PRE_OUT = 2;
+  float bpre[GB_PRE_OUT];
+#pragma unroll
+  for (int j = 0; j < GB_PRE_OUT; j++) {
+    const int o = crank * blockDim.x + threadIdx.x + j * kc * blockDim.x;
+    const int row = o / RC, col = o - row * RC, n = group * 128 + row;
+    bpre[j] = (o < 128 * RC && col < e.R && n < e.N) ? epi_bias(e, n) : 0.f;
+  }
   // LayerNorm gamma / beta of this K range: model data, staged before the wait
   float4* lnw = reinterpret_cast<float4*>(gb_smem + L.lnwb);
   float4* lnb = lnw + kn / 4;
@@ -163,6 +174,7 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
 
   // ---- activations of this K range (written by earlier kernels) ----
   pdl_wait();
+  const int pos = e.mode == EPI_QKV ? *e.pos : 0;
   const int xs_stride = pairs_per * 64 + 16;
   __half* xsm = reinterpret_cast<__half*>(gb_smem + L.xs);
   __half* xsm_lo = reinterpret_cast<__half*>(gb_smem + L.xs_lo);
@@ -269,12 +281,11 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
       red[(warp * 16 + g + 8 * (c >> 1)) * RC + nb * 8 + 2 * t + (c & 1)] = __fmaf_rn(acl[nb][c], SPLIT_INV, acc[nb][c]);
 
   // ---- sum the cluster's K ranges in rank order, store ----
-  cg::cluster_group cluster = cg::this_cluster();
   if (kc > 1) cluster.sync();
   else __syncthreads();
-  const int crank = kc > 1 ? (int)cluster.block_rank() : 0;
   if (*abort_flag == 0) {
-    for (int o = crank * blockDim.x + threadIdx.x; o < 128 * RC; o += kc * blockDim.x) {
+    int jo = 0;
+    for (int o = crank * blockDim.x + threadIdx.x; o < 128 * RC; o += kc * blockDim.x, jo++) {
       const int row = o / RC, col = o - row * RC;
       const int n = group * 128 + row;
       if (col >= e.R || n >= e.N) continue;
@@ -289,7 +300,12 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
       } else {
         v = red[o];
       }
-      epi_store(e, col, n, v);
+      float b;
+#pragma unroll
+      for (int j = 0; j < GB_PRE_OUT; j++)
+        if (jo == j) b = bpre[j];
+      if (jo >= GB_PRE_OUT) b = epi_bias(e, n);
+      epi_store_b(e, col, n, v, b, pos);
     }
   }
   if (kc > 1) cluster.sync();  // peers may still read this CTA's partial tile

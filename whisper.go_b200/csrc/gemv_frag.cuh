@@ -172,42 +172,64 @@ __device__ __forceinline__ void dequant_step_split(const Pay& p, int s, uint32_t
   }
 }
 
-__device__ __forceinline__ void epi_store(const Epi& e, int r, int n, float v) {
+// Bias added to output column n (model data, never written by the token
+// loop, so kernels may read it before their dependency wait).
+__device__ __forceinline__ float epi_bias(const Epi& e, int n) {
+  switch (e.mode) {
+    case EPI_QKV: {
+      const int seg = n / e.d, j = n - seg * e.d;
+      return seg == 0 ? e.bias_q[j] : (seg == 2 ? e.bias_v[j] : 0.f);
+    }
+    case EPI_CROSS_KV: {
+      const int lk = n / e.d, j = n - lk * e.d;
+      return (lk & 1) ? e.bias_v[(int64_t)(lk >> 1) * e.d + j] : 0.f;
+    }
+    default:
+      return e.bias ? e.bias[n] : 0.f;
+  }
+}
+
+// Stores v (+ bias b of column n) of activation row r; pos is the decode
+// position (*e.pos) for the KV-cache scatter of EPI_QKV.
+__device__ __forceinline__ void epi_store_b(const Epi& e, int r, int n, float v, float b, int pos) {
   switch (e.mode) {
     case EPI_F32:
-      if (e.bias) v = __fadd_rn(v, e.bias[n]);
+      if (e.bias) v = __fadd_rn(v, b);
       e.out[(int64_t)r * e.ldo + n] = v;
       break;
     case EPI_RESID: {
       // x += (acc + b): one writer per element, so the fire-and-forget
       // reduction rounds exactly like load-add-store without waiting on x
-      const float add = __fadd_rn(v, e.bias ? e.bias[n] : 0.f);
+      const float add = __fadd_rn(v, b);
       asm volatile("red.global.add.f32 [%0], %1;" ::"l"(e.out + (int64_t)r * e.ldo + n), "f"(add) : "memory");
       break;
     }
     case EPI_GELU_F16:
-      if (e.bias) v = __fadd_rn(v, e.bias[n]);
+      if (e.bias) v = __fadd_rn(v, b);
       e.out16[(int64_t)r * e.ldo + n] = __float2half_rn(gelu_f32(v));
       break;
     case EPI_QKV: {
       int seg = n / e.d, j = n - seg * e.d, h = j / e.hd, c = j - h * e.hd;
       if (seg == 0) {
-        e.out[(int64_t)r * e.ldo + j] = __fadd_rn(v, e.bias_q[j]);
+        e.out[(int64_t)r * e.ldo + j] = __fadd_rn(v, b);
       } else {
-        if (seg == 2) v = __fadd_rn(v, e.bias_v[j]);
-        int p = *e.pos;
-        e.kv[((((int64_t)r * 2 + (seg - 1)) * e.H + h) * e.T + p) * e.hd + c] = __float2half_rn(v);
+        if (seg == 2) v = __fadd_rn(v, b);
+        e.kv[((((int64_t)r * 2 + (seg - 1)) * e.H + h) * e.T + pos) * e.hd + c] = __float2half_rn(v);
       }
       break;
     }
     case EPI_CROSS_KV: {
       int u = r / e.T, tt = r - u * e.T;
       int lk = n / e.d, j = n - lk * e.d, l = lk >> 1, kv = lk & 1, h = j / e.hd, c = j - h * e.hd;
-      if (kv) v = __fadd_rn(v, e.bias_v[(int64_t)l * e.d + j]);
+      if (kv) v = __fadd_rn(v, b);
       e.kv[(((((int64_t)l * e.U + u) * 2 + kv) * e.H + h) * e.T + tt) * e.hd + c] = __float2half_rn(v);
       break;
     }
   }
+}
+
+__device__ __forceinline__ void epi_store(const Epi& e, int r, int n, float v) {
+  epi_store_b(e, r, n, v, epi_bias(e, n), e.mode == EPI_QKV ? *e.pos : 0);
 }
 
 }  // namespace
