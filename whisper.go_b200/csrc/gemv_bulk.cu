@@ -63,6 +63,43 @@ __host__ __device__ inline GbLayout gb_layout(uint32_t qt, int np, int RC) {
 
 constexpr int LN_MAX_NV = 10;  // float4 runs per lane of the vec layout (d <= 1280)
 
+// Mean and standard deviation of a row held in registers in the vec layout
+// (float4 runs lane + 32 j, j < nv): the arithmetic of layernorm_reg_kernel.
+__device__ __forceinline__ void ln_stats_regs(const float4* v, int nv, int d, float& mean, float& sd) {
+  float s = 0.f, q = 0.f;
+#pragma unroll
+  for (int j = 0; j < LN_MAX_NV; j++)
+    if (j < nv) s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+  s = warp_sum(s);
+  mean = __fdiv_rn(s, (float)d);
+#pragma unroll
+  for (int j = 0; j < LN_MAX_NV; j++) {
+    if (j < nv) {
+      const float a = __fsub_rn(v[j].x, mean), b = __fsub_rn(v[j].y, mean), c = __fsub_rn(v[j].z, mean),
+                  e = __fsub_rn(v[j].w, mean);
+      q = __fmaf_rn(a, a, q);
+      q = __fmaf_rn(b, b, q);
+      q = __fmaf_rn(c, c, q);
+      q = __fmaf_rn(e, e, q);
+    }
+  }
+  q = warp_sum(q);
+  sd = __fsqrt_rn(__fadd_rn(__fdiv_rn(q, (float)d), 1e-5f));
+}
+
+// LayerNorm output o as f16 hi + lo / 2^10 (both f16): the products keep
+// ~22 bits of the float32 activation. Writes 4 adjacent halves of each part.
+__device__ __forceinline__ void ln_store_split(__half* hi, __half* lo, const float* o) {
+  const __half2 h0 = __floats2half2_rn(o[0], o[1]), h1 = __floats2half2_rn(o[2], o[3]);
+  const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+  const __half2 l0 = __floats2half2_rn(__fmul_rn(__fsub_rn(o[0], f0.x), SPLIT_SCALE),
+                                       __fmul_rn(__fsub_rn(o[1], f0.y), SPLIT_SCALE));
+  const __half2 l1 = __floats2half2_rn(__fmul_rn(__fsub_rn(o[2], f1.x), SPLIT_SCALE),
+                                       __fmul_rn(__fsub_rn(o[3], f1.y), SPLIT_SCALE));
+  *reinterpret_cast<uint2*>(hi) = make_uint2(h2_as_u32(h0), h2_as_u32(h1));
+  *reinterpret_cast<uint2*>(lo) = make_uint2(h2_as_u32(l0), h2_as_u32(l1));
+}
+
 // Mean and standard deviation of one row of d floats by one warp, with the
 // arithmetic of the LayerNorm kernels (internal/ml/ops.go:153-202): vec —
 // per-lane float4 runs lane + 32 i (layernorm_reg_kernel), else lane-strided
@@ -179,13 +216,46 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
   __half* xsm = reinterpret_cast<__half*>(gb_smem + L.xs);
   __half* xsm_lo = reinterpret_cast<__half*>(gb_smem + L.xs_lo);
   const bool x_split = e.ln_x != nullptr;  // the activations have a lo part
-  if (e.ln_x) {
-    // fused LayerNorm: every CTA takes the statistics of the (<= 16) rows
+  if (e.ln_x && ln_vec) {
+    // fused LayerNorm, vec layout (d = 128 nv): warp w loads rows w, w + 8,
+    // ... into registers (one L2 round trip), takes their statistics and
+    // normalises the elements of this CTA's K range straight from the
+    // registers, element by element as the LayerNorm kernel does
+    const int nv = e.ln_d >> 7;
+    for (int rr = warp; rr < RC; rr += GB_WARPS) {
+      if (rr < e.R) {
+        const float4* x4 = reinterpret_cast<const float4*>(e.ln_x + (int64_t)rr * e.ln_d);
+        float4 v[LN_MAX_NV];
+#pragma unroll
+        for (int j = 0; j < LN_MAX_NV; j++)
+          if (j < nv) v[j] = x4[lane + 32 * j];
+        float mean, sd;
+        ln_stats_regs(v, nv, e.ln_d, mean, sd);
+#pragma unroll
+        for (int j = 0; j < LN_MAX_NV; j++) {
+          const int kk = 4 * (lane + 32 * j) - k0;
+          if (j < nv && kk >= 0 && kk < kn) {
+            const float4 w = lnw[kk / 4], b = lnb[kk / 4];
+            float o[4];
+            o[0] = __fadd_rn(__fdiv_rn(__fmul_rn(w.x, __fsub_rn(v[j].x, mean)), sd), b.x);
+            o[1] = __fadd_rn(__fdiv_rn(__fmul_rn(w.y, __fsub_rn(v[j].y, mean)), sd), b.y);
+            o[2] = __fadd_rn(__fdiv_rn(__fmul_rn(w.z, __fsub_rn(v[j].z, mean)), sd), b.z);
+            o[3] = __fadd_rn(__fdiv_rn(__fmul_rn(w.w, __fsub_rn(v[j].w, mean)), sd), b.w);
+            ln_store_split(xsm + rr * xs_stride + kk, xsm_lo + rr * xs_stride + kk, o);
+          }
+        }
+      } else {
+        const float z[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int kk = 4 * lane; kk < kn; kk += 128) ln_store_split(xsm + rr * xs_stride + kk, xsm_lo + rr * xs_stride + kk, z);
+      }
+    }
+  } else if (e.ln_x) {
+    // fused LayerNorm, other d: every CTA takes the statistics of the rows
     // and normalises its own K range, element by element as the kernel does
     float* stat = reinterpret_cast<float*>(gb_smem + L.stat);
     for (int rr = warp; rr < e.R; rr += GB_WARPS) {
       float mean, sd;
-      ln_row_stats(e.ln_x + (int64_t)rr * e.ln_d, e.ln_d, ln_vec != 0, lane, mean, sd);
+      ln_row_stats(e.ln_x + (int64_t)rr * e.ln_d, e.ln_d, false, lane, mean, sd);
       if (lane == 0) {
         stat[2 * rr] = mean;
         stat[2 * rr + 1] = sd;
@@ -207,16 +277,7 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
         o[2] = __fadd_rn(__fdiv_rn(__fmul_rn(w.z, __fsub_rn(x.z, mean)), sd), b.z);
         o[3] = __fadd_rn(__fdiv_rn(__fmul_rn(w.w, __fsub_rn(x.w, mean)), sd), b.w);
       }
-      // LayerNorm output as hi + lo / 2^10 (both f16): the products keep
-      // ~22 bits of the float32 activation
-      const __half2 h0 = __floats2half2_rn(o[0], o[1]), h1 = __floats2half2_rn(o[2], o[3]);
-      const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
-      const __half2 l0 = __floats2half2_rn(__fmul_rn(__fsub_rn(o[0], f0.x), SPLIT_SCALE),
-                                           __fmul_rn(__fsub_rn(o[1], f0.y), SPLIT_SCALE));
-      const __half2 l1 = __floats2half2_rn(__fmul_rn(__fsub_rn(o[2], f1.x), SPLIT_SCALE),
-                                           __fmul_rn(__fsub_rn(o[3], f1.y), SPLIT_SCALE));
-      *reinterpret_cast<uint2*>(xsm + rr * xs_stride + kk) = make_uint2(h2_as_u32(h0), h2_as_u32(h1));
-      *reinterpret_cast<uint2*>(xsm_lo + rr * xs_stride + kk) = make_uint2(h2_as_u32(l0), h2_as_u32(l1));
+      ln_store_split(xsm + rr * xs_stride + kk, xsm_lo + rr * xs_stride + kk, o);
     }
   } else {
     const int cpr = kn / 8;
