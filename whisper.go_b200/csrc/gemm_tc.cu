@@ -596,12 +596,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (r >= R) break;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       if (ks > 1) {
-        for (int k = 0; k < ks; k++) {  // rank order
-          const float4 p4 = __ldcg(reinterpret_cast<const float4*>(part + ((size_t)k * NR + row_lo + jr) * 128) + lane);
-          acc.x += p4.x;
-          acc.y += p4.y;
-          acc.z += p4.z;
-          acc.w += p4.w;
+        // the ks (<= 8) partials of the row are loaded together, then
+        // summed in rank order
+        float4 p4[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+          if (k < ks) p4[k] = __ldcg(reinterpret_cast<const float4*>(part + ((size_t)k * NR + row_lo + jr) * 128) + lane);
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+          if (k < ks) {
+            acc.x += p4[k].x;
+            acc.y += p4[k].y;
+            acc.z += p4[k].z;
+            acc.w += p4[k].w;
+          }
         }
       } else {
         acc = reinterpret_cast<const float4*>(part + (size_t)jr * 128)[lane];
