@@ -216,6 +216,8 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
   __half* xsm = reinterpret_cast<__half*>(gb_smem + L.xs);
   __half* xsm_lo = reinterpret_cast<__half*>(gb_smem + L.xs_lo);
   const bool x_split = e.ln_x != nullptr;  // the activations have a lo part
+  // gamma / beta were staged by other threads of the CTA
+  if (e.ln_x) __syncthreads();
   if (e.ln_x && ln_vec) {
     // fused LayerNorm, vec layout (d = 128 nv): warp w loads rows w, w + 8,
     // ... into registers (one L2 round trip), takes their statistics and

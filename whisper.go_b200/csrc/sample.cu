@@ -767,7 +767,12 @@ __global__ void __launch_bounds__(128) beam_update_kernel(SampleState s) {
   }
   __syncthreads();
   const int nc = nc_sh;
-  // stable rank by normScore (descending)
+  // stable rank by normScore (descending). A NaN score ranks as -inf, so the
+  // ranks are a permutation of the candidates whatever the values (with NaN
+  // left in, every NaN candidate would rank first and ranks would go unset).
+  for (int i = threadIdx.x; i < nc; i += blockDim.x)
+    if (c_norm[i] != c_norm[i]) c_norm[i] = -INFINITY;
+  __syncthreads();
   for (int i = threadIdx.x; i < nc; i += blockDim.x) {
     int rank = 0;
     for (int j = 0; j < nc; j++) rank += (c_norm[j] > c_norm[i]) || (c_norm[j] == c_norm[i] && j < i);
