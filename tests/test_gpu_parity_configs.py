@@ -136,6 +136,58 @@ def test_teacher_forced_batched_rows(name, U, n, check):
         m.close()
 
 
+def test_beam_decode_config3_shape():
+    """Config 3's shape and quantisation (d 768, 12 heads, 12 layers, Q5_1,
+    odd vocabulary) with beam 5 at one utterance: the batch-1 kernels through
+    the job API and the CUDA graph for a full 224-step decode, twice. Every
+    token must be in the vocabulary and the two decodes identical (a race in
+    a kernel shows up as a difference, or as garbage tokens); the first steps
+    are compared with the oracle beam by beam."""
+    m = synthetic("c3")
+    dec = wgdec.WhisperDecoder(m)
+    try:
+        enc = m.encoder_output(5)
+        params = wgdec.DecoderParams(prompt=PROMPT, beam_size=5, max_tokens=224, suppress_eot=True,
+                                     mode=wgdec.MODE_CORRECT)
+        t1, l1, s1 = dec.decode_tokens([enc], params)
+        t2, l2, s2 = dec.decode_tokens([enc], params)
+        n = int(l1[0])
+        assert len(PROMPT) < n <= len(PROMPT) + 224
+        assert np.all((t1[0, :n] >= 0) & (t1[0, :n] < m.n_vocab))
+        np.testing.assert_array_equal(l1, l2)
+        np.testing.assert_array_equal(t1, t2)
+        np.testing.assert_array_equal(s1, s2)
+        assert np.isfinite(s1[0])
+        B, M = 5, 6
+        short = wgdec.DecoderParams(prompt=PROMPT, beam_size=B, max_tokens=M, suppress_eot=True,
+                                    mode=wgdec.MODE_CORRECT)
+        tr = oracle.decode_trace(m, [enc], short, m.n_ctx, threads=THREADS)
+        job = wgdec.Job(dec, 1, enc.shape[0], short)
+        try:
+            job.upload([enc])
+            job.start()
+            for st in range(M):
+                done = job.step(1)
+                toks, lens, scores = job.beams()
+                if st >= tr["steps"][0]:
+                    break
+                same = lens[0].tolist() == tr["beams_lens"][0, st].tolist() and all(
+                    toks[0, b, :lens[0, b]].tolist() == tr["beams_tokens"][0, st, b, :lens[0, b]].tolist()
+                    for b in range(B))
+                if not same:
+                    assert tr["margins"][0, st] <= MARGIN, \
+                        "step %d: beams differ at margin %.3g" % (st, tr["margins"][0, st])
+                    break
+                np.testing.assert_allclose(scores[0], tr["beams_scores"][0, st], atol=2e-2)
+                if done:
+                    break
+        finally:
+            job.close()
+    finally:
+        dec.close()
+        m.close()
+
+
 # ---- token decisions at many rows ------------------------------------------------------
 @pytest.fixture(scope="module")
 def wide():
