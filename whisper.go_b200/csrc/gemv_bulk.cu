@@ -203,11 +203,15 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
   // LayerNorm gamma / beta of this K range: model data, staged before the wait
   float4* lnw = reinterpret_cast<float4*>(gb_smem + L.lnwb);
   float4* lnb = lnw + kn / 4;
-  if (e.ln_x)
+  if (e.ln_x) {
     for (int i = threadIdx.x; i < kn / 4; i += blockDim.x) {
       lnw[i] = reinterpret_cast<const float4*>(e.ln_w + k0)[i];
       lnb[i] = reinterpret_cast<const float4*>(e.ln_b + k0)[i];
     }
+    // every warp reads elements other threads staged; the barrier sits before
+    // the dependency wait, where the CTA waits for its predecessor anyway
+    __syncthreads();
+  }
 
   // ---- activations of this K range (written by earlier kernels) ----
   pdl_wait();
@@ -216,8 +220,6 @@ __global__ void __launch_bounds__(GB_WARPS * 32)
   __half* xsm = reinterpret_cast<__half*>(gb_smem + L.xs);
   __half* xsm_lo = reinterpret_cast<__half*>(gb_smem + L.xs_lo);
   const bool x_split = e.ln_x != nullptr;  // the activations have a lo part
-  // gamma / beta were staged by other threads of the CTA
-  if (e.ln_x) __syncthreads();
   if (e.ln_x && ln_vec) {
     // fused LayerNorm, vec layout (d = 128 nv): warp w loads rows w, w + 8,
     // ... into registers (one L2 round trip), takes their statistics and
