@@ -361,6 +361,7 @@ int forward_step(wg_model* m, DevJob& j, const int* tokens, bool want_logits, in
   for (int l = 0; l < m->L; l++) {
     const DevLayer& ly = dm.layers[l];
     __half* kv = j.selfkv + l * layer_kv;
+    NvtxRange layer_range("decoder layer");
     // self-attention (decoder.go:836-908)
     Epi e = job_epi(j);
     WG_CHECK(norm_for(ly.qkv, ly.sln_w, ly.sln_b, e));
@@ -394,6 +395,7 @@ int forward_step(wg_model* m, DevJob& j, const int* tokens, bool want_logits, in
     WG_CHECK(launch_matmul(ly.m2, j.h16, j.ld4, R, e, st));
   }
   if (!want_logits) return WG_OK;
+  NvtxRange logits_range("final LayerNorm + logits");
   Epi e = job_epi(j);
   WG_CHECK(norm_for(dm.tok, dm.ln_w, dm.ln_b, e));  // decoder.go:818
   e.mode = EPI_F32; e.out = j.logits; e.ldo = m->V; e.N = m->V;
@@ -596,6 +598,7 @@ int start_devjob(wg_job* J, DevJob& j) {
 
 int step_eager(wg_job* J, DevJob& j) {
   WG_CHECK(forward_step(J->m, j, j.ss.tok_in, true, J->mode));
+  NvtxRange sample_range("sampling");
   return launch_sample_step(j.ss, j.st);
 }
 
@@ -906,7 +909,11 @@ int wg_job_start(wg_job* J) {
       set_error("model: decode: injected fault on device %d", j.dev);
       return WG_ERR_INJECTED;
     }
-    WG_CHECK(start_devjob(J, j));
+    {
+      NvtxRange r("job start: encoder f16, cross K/V precompute, prompt prefill");
+      WG_CHECK(start_devjob(J, j));
+    }
+    NvtxRange r("token-step graph capture");
     WG_CHECK(ensure_graph(J, j));
   }
   for (DevJob* j : J->dj) {
@@ -948,6 +955,7 @@ int wg_job_step(wg_job* J, int max_steps, int* done) {
       set_error("model: decode: injected fault at step %d", J->steps_done);
       return WG_ERR_INJECTED;
     }
+    NvtxRange step_range("token step");
     for (DevJob* j : J->dj) {
       WG_CHECK_CUDA(cudaSetDevice(j->dev));
       if (j->graph) {

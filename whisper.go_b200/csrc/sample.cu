@@ -739,30 +739,43 @@ __global__ void __launch_bounds__(128) beam_update_kernel(SampleState s) {
   __shared__ int c_parent[MAXB * TOPK], c_tok[MAXB * TOPK];
   __shared__ int nc_sh;
   __shared__ int sel[MAXB];
-  if (threadIdx.x == 0) {
-    int nc = 0;
-    for (int b = 0; b < B; b++) {
-      int r = u * B + b;
-      int n = s.len[r];
-      const int* h = s.hist + (int64_t)r * s.Tcap;
-      float sc = s.score[r];
-      if (n > 0 && h[n - 1] == s.eot) {
-        c_parent[nc] = b; c_score[nc] = sc; c_tok[nc] = s.eot; c_lp[nc] = 0.f;
-        c_norm[nc] = __fdiv_rn(sc, (float)pow((double)n, 0.6));
-        nc++;
-        continue;
-      }
-      float den = (float)pow((double)(n + 1), 0.6);
-      for (int j = 0; j < TOPK; j++) {
-        int tk = s.topk_tok[r * TOPK + j];
+  __shared__ int b_cnt[MAXB];
+  // candidates of beam b (thread b, all beams at once) into slots
+  // b*TOPK .. b*TOPK+TOPK-1, then compacted in beam order by one thread
+  if (threadIdx.x < B) {
+    const int b = threadIdx.x, r = u * B + b, base = b * TOPK;
+    const int n = s.len[r];
+    const int* h = s.hist + (int64_t)r * s.Tcap;
+    const float sc = s.score[r];
+    int k = 0;
+    if (n > 0 && h[n - 1] == s.eot) {
+      c_parent[base] = b; c_score[base] = sc; c_tok[base] = s.eot; c_lp[base] = 0.f;
+      c_norm[base] = __fdiv_rn(sc, (float)pow((double)n, 0.6));
+      k = 1;
+    } else {
+      const float den = (float)pow((double)(n + 1), 0.6);
+      for (int jj = 0; jj < TOPK; jj++) {
+        const int tk = s.topk_tok[r * TOPK + jj];
         if (tk < 0) continue;
-        float lp = s.topk_lp[r * TOPK + j];
-        float ns = __fadd_rn(sc, lp);
-        c_parent[nc] = b; c_score[nc] = ns; c_tok[nc] = tk; c_lp[nc] = lp;
-        c_norm[nc] = __fdiv_rn(ns, den);
-        nc++;
+        const float lp = s.topk_lp[r * TOPK + jj];
+        const float ns = __fadd_rn(sc, lp);
+        c_parent[base + k] = b; c_score[base + k] = ns; c_tok[base + k] = tk; c_lp[base + k] = lp;
+        c_norm[base + k] = __fdiv_rn(ns, den);
+        k++;
       }
     }
+    b_cnt[b] = k;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int nc = 0;  // in place: a candidate only moves to a lower slot
+    for (int b = 0; b < B; b++)
+      for (int k = 0; k < b_cnt[b]; k++, nc++) {
+        const int src = b * TOPK + k;
+        if (src == nc) continue;
+        c_parent[nc] = c_parent[src]; c_score[nc] = c_score[src]; c_tok[nc] = c_tok[src];
+        c_lp[nc] = c_lp[src]; c_norm[nc] = c_norm[src];
+      }
     nc_sh = nc;
   }
   __syncthreads();
